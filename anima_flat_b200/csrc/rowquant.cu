@@ -1,0 +1,209 @@
+// Per-row FP8 e4m3 quantisation, optionally after GELU.
+//
+// Reference: src/kernels/fp8.py:273-292 (_rowquant_kernel) and :260-270
+// (_gelu, Abramowitz & Stegun 7.1.26).  Per row of K elements:
+//   y = gelu(x) if GELU else x                     (fp32)
+//   s = max(max|y|, 1e-12) / 448;  q = e4m3(clamp(y / s, +-448))
+//
+// Layout: a group of GROUP warps owns a row; thread t of the group holds the
+// 16-element chunks ch = t + 32*GROUP*c (c < CPL), i.e. two 16-byte loads and
+// one 16-byte FP8 store per chunk.  The amax is a max, so the order of the
+// reduction does not matter.
+//
+// Without GELU every operation is IEEE (q = y / s by division), so codes and
+// scales are exact.  With GELU the per-element work would make the kernel
+// compute-bound, so the codes use fast_gelu() and y * (1 / s); the scale stays
+// exact: every element whose fast value lies within the fast_gelu error bound
+// of the row's fast amax is recomputed with canonical_gelu() and the exact
+// amax is the max over those candidates.  The codes can then differ from the
+// canonical ones only where y / s lies within a few fp32 ulps of an e4m3
+// rounding tie.
+#include "afb_device.cuh"
+#include "afb_launch.h"
+
+namespace afb {
+
+// Out of line: the candidate branch is rare and the row loop is unrolled.
+__device__ __noinline__ float canonical_gelu_call(float x) { return canonical_gelu(x); }
+
+struct RowquantArgs {
+  const uint16_t* x;  // [rows, K] bf16
+  uint8_t* q;         // [rows, K] e4m3
+  float* s;           // [rows] fp32
+  int64_t rows;
+  int K;
+};
+
+template <int CPL, int GROUP, bool GELU>
+__global__ void __launch_bounds__(kRowWarps * 32)
+rowquant_kernel(const RowquantArgs a) {
+  static_assert(kRowWarps % GROUP == 0, "GROUP must divide the CTA's warps");
+  __shared__ float red[kRowWarps];
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int t = (warp % GROUP) * 32 + lane;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowWarps / GROUP) + warp / GROUP;
+  const bool row_ok = row < a.rows;
+  const int K = a.K;
+  const int64_t base = (row_ok ? row : 0) * K;
+
+  uint4 xv[CPL][2];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) {
+    const int e = (t + 32 * GROUP * c) * 16;
+    const bool ok = row_ok && e < K;
+    xv[c][0] = ok ? ld_stream(a.x + base + e) : make_uint4(0, 0, 0, 0);
+    xv[c][1] = ok ? ld_stream(a.x + base + e + 8) : make_uint4(0, 0, 0, 0);
+  }
+
+  float y[CPL][16];
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) {
+    float lo[8], hi[8];
+    unpack8(xv[c][0], lo);
+    unpack8(xv[c][1], hi);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      y[c][k] = GELU ? fast_gelu(lo[k]) : lo[k];
+      y[c][k + 8] = GELU ? fast_gelu(hi[k]) : hi[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(y[c][k]));
+  }
+
+  // Group-wide max.  Padding elements are zero and leave the max unchanged.
+  auto group_max = [&](float v) {
+    v = warp_max(v);
+    if (GROUP > 1) {
+      __syncthreads();
+      if (lane == 0) red[warp] = v;
+      __syncthreads();
+      const int w0 = (warp / GROUP) * GROUP;
+#pragma unroll
+      for (int w = 0; w < GROUP; ++w) v = fmaxf(v, red[w0 + w]);
+    }
+    return v;
+  };
+  amax = group_max(amax);
+
+  if (GELU) {
+    // Exact amax over the candidates (see the file comment).
+    const float margin = __fmaf_rn(amax, 0x1p-11f, 0x1p-19f);
+    const float thresh = amax - margin;
+    float exact = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        if (fabsf(y[c][k]) >= thresh) {
+          const float xk = unpack_at(xv[c][k >> 3], k & 7);
+          exact = fmaxf(exact, fabsf(canonical_gelu_call(xk)));
+        }
+      }
+    }
+    amax = group_max(exact);
+  }
+
+  const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
+  const float r = __fdiv_rn(1.0f, s);
+  if (!row_ok) return;
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) {
+    const int e = (t + 32 * GROUP * c) * 16;
+    if (e < K) {
+      float lo[8], hi[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float vlo = GELU ? __fmul_rn(y[c][k], r) : __fdiv_rn(y[c][k], s);
+        const float vhi = GELU ? __fmul_rn(y[c][k + 8], r) : __fdiv_rn(y[c][k + 8], s);
+        lo[k] = fminf(fmaxf(vlo, -448.0f), 448.0f);
+        hi[k] = fminf(fmaxf(vhi, -448.0f), 448.0f);
+      }
+      const uint2 plo = e4m3x8(lo);
+      const uint2 phi = e4m3x8(hi);
+      st16(a.q + base + e, make_uint4(plo.x, plo.y, phi.x, phi.y));
+    }
+  }
+  if (t == 0) a.s[row] = s;
+}
+
+// Threads-per-row grouping and chunks per thread for a row of K elements.
+static bool rowquant_shape(int64_t K, int* group, int* cpl) {
+  const int64_t chunks = (K + 15) / 16;
+  if (chunks <= 32 * 4) {
+    *group = 1;
+    *cpl = chunks <= 32 ? 1 : chunks <= 64 ? 2 : 4;
+    return true;
+  }
+  if (chunks <= 128 * 8) {
+    *group = 4;
+    *cpl = chunks <= 128 * 2 ? 2 : chunks <= 128 * 4 ? 4 : 8;
+    return true;
+  }
+  return false;
+}
+
+template <bool GELU>
+static cudaError_t launch_rowquant(const RowquantArgs& a, cudaStream_t st) {
+  int group = 0, cpl = 0;
+  if (!rowquant_shape(a.K, &group, &cpl)) return cudaErrorInvalidValue;
+  const int rows_per_cta = kRowWarps / group;
+  const dim3 grid(static_cast<unsigned>((a.rows + rows_per_cta - 1) / rows_per_cta));
+  const dim3 block(kRowWarps * 32);
+  if (group == 1) {
+    switch (cpl) {
+      case 1: return launch_pdl(rowquant_kernel<1, 1, GELU>, grid, block, 0, st, a);
+      case 2: return launch_pdl(rowquant_kernel<2, 1, GELU>, grid, block, 0, st, a);
+      default: return launch_pdl(rowquant_kernel<4, 1, GELU>, grid, block, 0, st, a);
+    }
+  }
+  switch (cpl) {
+    case 2: return launch_pdl(rowquant_kernel<2, 4, GELU>, grid, block, 0, st, a);
+    case 4: return launch_pdl(rowquant_kernel<4, 4, GELU>, grid, block, 0, st, a);
+    default: return launch_pdl(rowquant_kernel<8, 4, GELU>, grid, block, 0, st, a);
+  }
+}
+
+// Elementwise fast and canonical GELU, for checking the fast_gelu error bound
+// that the GELU row kernel relies on.
+__global__ void gelu_probe_kernel(const uint16_t* x, float* fast, float* canon, int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = __uint_as_float(static_cast<uint32_t>(x[i]) << 16);
+  fast[i] = fast_gelu(v);
+  canon[i] = canonical_gelu(v);
+}
+
+}  // namespace afb
+
+using namespace afb;
+
+extern "C" int afb_rowquant(const void* x, void* q, void* s, int64_t rows, int64_t K, int gelu,
+                            void* stream) {
+  ApiGuard g("afb_rowquant");
+  int group = 0, cpl = 0;
+  if (!check(rows >= 0, "rows must be >= 0") ||
+      !check(K >= 16 && K % 16 == 0 && rowquant_shape(K, &group, &cpl),
+             "K must be a multiple of 16 in [16, 16384], got " + std::to_string(K)) ||
+      !check_ptrs({x, q}, {"x", "q"}) || !check_ptr4(s, "s"))
+    return g.fail();
+  if (rows == 0) return 0;
+  RowquantArgs a{static_cast<const uint16_t*>(x), static_cast<uint8_t*>(q),
+                 static_cast<float*>(s), rows, static_cast<int>(K)};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return g.done(gelu ? launch_rowquant<true>(a, st) : launch_rowquant<false>(a, st));
+}
+
+extern "C" int afb_gelu_probe(const void* x, void* fast, void* canon, int64_t n, void* stream) {
+  ApiGuard g("afb_gelu_probe");
+  if (!check(n >= 0, "n must be >= 0") || !check_ptrs({x, fast, canon}, {"x", "fast", "canon"}))
+    return g.fail();
+  if (n == 0) return 0;
+  gelu_probe_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                      static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), static_cast<float*>(fast), static_cast<float*>(canon), n);
+  return g.done(cudaGetLastError());
+}

@@ -1,0 +1,103 @@
+"""The fused-op call sequence of one denoiser forward, and its byte model.
+
+Mirrors the order in which the reference's ``AnimaFlat.forward_fused``
+(src/model.py:339-376, per block ``_fused_block`` :297-337) and
+``forward_fp8`` (:403-473) call the hot-path ops, so that a benchmark step
+launches exactly the ops, shapes and counts of one forward pass.  GEMMs and
+attention between the ops are not part of the path; their outputs are
+stand-in input buffers.
+
+Algorithmic bytes count every activation read and written once per call plus
+the per-call parameter vectors and tables (the §(d) byte model): they are the
+numerator of the reported HBM GB/s.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+
+@dataclass(frozen=True)
+class Shape:
+    batch: int = 1
+    seq: int = 4096
+    dim: int = 2048
+    heads: int = 16
+    head_dim: int = 128
+    layers: int = 28
+    mlp: int = 8192
+
+    @property
+    def rows(self) -> int:
+        return self.batch * self.seq
+
+
+def bytes_residual_adaln(s: Shape) -> int:
+    return s.rows * s.dim * 2 * 4 + 3 * s.batch * s.dim * 2
+
+
+def bytes_adaln(s: Shape) -> int:
+    return s.rows * s.dim * 2 * 2 + 2 * s.batch * s.dim * 2
+
+
+def bytes_qkv_norm_rope(s: Shape, with_v: bool = False) -> int:
+    w = s.heads * s.head_dim
+    per_row = (2 * w + 2 * w) * 2 + (2 * w * 2 if with_v else 0)
+    tables = 2 * s.seq * (s.head_dim // 2) * 4
+    return s.rows * per_row + tables + 2 * s.head_dim * 4
+
+
+def bytes_head_norm(s: Shape) -> int:
+    return s.rows * s.heads * s.head_dim * 2 * 2 + s.head_dim * 4
+
+
+def bytes_residual_adaln_fp8(s: Shape) -> int:
+    return s.rows * (s.dim * 2 * 3 + s.dim + 4) + 3 * s.batch * s.dim * 2
+
+
+def bytes_adaln_fp8(s: Shape) -> int:
+    return s.rows * (s.dim * 2 + s.dim + 4) + 2 * s.batch * s.dim * 2
+
+
+def bytes_rowquant(s: Shape, K: int) -> int:
+    return s.rows * (K * 2 + K + 4)
+
+
+def bf16_forward_calls(s: Shape) -> list[str]:
+    """Op names in call order for forward_fused (model.py:366-375)."""
+    calls = ["adaln"]
+    for layer in range(s.layers):
+        calls += ["qkv_norm_rope", "residual_adaln", "head_norm", "residual_adaln"]
+        if layer + 1 < s.layers:
+            calls.append("residual_adaln")
+    calls.append("residual_adaln")  # final layer (model.py:375)
+    return calls
+
+
+def fp8_forward_calls(s: Shape) -> list[str]:
+    """Op names in call order for forward_fp8 (model.py:434-472)."""
+    calls = ["adaln_fp8"]
+    for layer in range(s.layers):
+        calls += ["qkv_norm_rope", "rowquant", "residual_adaln_fp8", "head_norm", "rowquant",
+                  "residual_adaln_fp8", "rowquant_gelu"]
+        if layer + 1 < s.layers:
+            calls.append("residual_adaln_fp8")
+    calls.append("residual_adaln")
+    return calls
+
+
+def call_bytes(name: str, s: Shape) -> int:
+    return {
+        "adaln": bytes_adaln,
+        "residual_adaln": bytes_residual_adaln,
+        "qkv_norm_rope": bytes_qkv_norm_rope,
+        "head_norm": bytes_head_norm,
+        "adaln_fp8": bytes_adaln_fp8,
+        "residual_adaln_fp8": bytes_residual_adaln_fp8,
+        "rowquant": lambda sh: bytes_rowquant(sh, sh.dim),
+        "rowquant_gelu": lambda sh: bytes_rowquant(sh, sh.mlp),
+    }[name](s)
+
+
+def step_bytes(calls: list[str], s: Shape) -> int:
+    return sum(call_bytes(c, s) for c in calls)

@@ -1,0 +1,587 @@
+"""Benchmark of the fused layer-op hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2|cfg3]
+
+A step is one pass of the hot path over one batch: the fused-op sequence of
+one Cosmos-Predict2-2B denoiser forward at 1024x1024 (config 2: B=1,
+S=4096, D=2048, 16 heads x 128; 1 adaln + 28 x [qkv_norm_rope,
+residual_adaln, head_norm, residual_adaln, residual_adaln] + the final
+residual_adaln = 141 launches), in the call order of the reference's
+forward_fused (src/model.py:339-376).  ``--workload cfg3`` runs the FP8
+forward sequence (forward_fp8, model.py:403-473) at B=2.
+
+Every call reads its own freshly generated input buffers (the step's working
+set is several GB, far above the 126 MB L2), so no input is served from L2
+by an earlier call; between steps the same holds.  The step is captured in a
+CUDA graph and launched with programmatic dependent launch.
+
+value: algorithmic HBM bytes of all ranks' steps / max-over-ranks device
+time (CUDA events), in GB/s.  e2e: the same metric through the public API
+with pinned host buffers, host<->device copies inside the timed region.
+roofline: the dominant kernel (residual_adaln) timed per launch with CUDA
+events recorded inside an instrumented copy of the step graph.
+cpu_baseline: the reference's unfused torch fp32 eager composition on the
+host cores (rank 0, N=1), on a bounded sample (config-1 shapes).
+
+Multi-GPU: one process per GPU (torchrun), each rank runs the same per-rank
+workload on its own sequences (weak scaling); no collective on the data path.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from anima_flat_b200 import workload as W  # noqa: E402
+
+METRIC = "fused AdaLN/RMSNorm/RoPE HBM GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ----------------------------------------------------------------- helpers --
+def peak_hbm() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback (profiling recipe, 6.65 TB/s)"
+
+
+def ncu_traffic(kernel_key: str):
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    try:
+        return json.loads(p.read_text())[kernel_key]
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        loaded = [v for v in sm if v > 0]
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def dist_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ------------------------------------------------------------- the step --
+class Step:
+    """Inputs, outputs and launch order of one forward's fused-op sequence."""
+
+    def __init__(self, shape: W.Shape, fp8: bool, device, seed: int):
+        import anima_flat_b200 as afb
+
+        self.afb = afb
+        self.s = shape
+        self.fp8 = fp8
+        self.calls = W.fp8_forward_calls(shape) if fp8 else W.bf16_forward_calls(shape)
+        self.bytes = W.step_bytes(self.calls, shape)
+        s = shape
+        g = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+
+        def act(*dims):
+            return torch.randn(*dims, generator=g, device=device, dtype=torch.float32).to(bf)
+
+        B, S, D, H, hd, L = s.batch, s.seq, s.dim, s.heads, s.head_dim, s.layers
+        self.mod = (torch.randn(L, 3, 3, B, D, generator=g, device=device) * 0.1).to(bf)
+        self.mod[:, :, 1] += 1.0
+        self.fin = (torch.randn(B, 2 * D, generator=g, device=device) * 0.1).to(bf)
+        side = int(round(S ** 0.5))
+        self.cos, self.sin = afb.rope_tables(side, S // side, hd, device, (4.0, 4.0))
+        self.qw = [1.0 + 0.02 * torch.randn(hd, generator=g, device=device) for _ in range(L)]
+        self.kw = [1.0 + 0.02 * torch.randn(hd, generator=g, device=device) for _ in range(L)]
+        self.xw = [1.0 + 0.02 * torch.randn(hd, generator=g, device=device) for _ in range(L)]
+        # Distinct inputs per call: the residual stream too, so that no call reads
+        # data a previous call left in L2.
+        self.z0 = act(B, S, D)
+        self.qkv = [act(B, S, 3 * H * hd) for _ in range(L)]
+        self.sub = [[act(B, S, D) for _ in range(3)] for _ in range(L)]   # o1, o2, mlp out
+        self.res = [[act(B, S, D) for _ in range(3)] for _ in range(L)]
+        self.xq = [act(B, S, D) for _ in range(L)]
+        if fp8:
+            self.attn = [[act(B, S, D) for _ in range(2)] for _ in range(L)]
+            self.up = [act(B, S, s.mlp) for _ in range(L)]
+        self.timed = "residual_adaln_fp8" if fp8 else "residual_adaln"
+        self.timed_hook = None  # called around launches of self.timed when instrumenting
+
+    def _op(self, name, fn, *a, **kw):
+        hook = self.timed_hook if name == self.timed else None
+        if hook is not None:
+            hook(True)
+        out = fn(*a, **kw)
+        if hook is not None:
+            hook(False)
+        return out
+
+    def block_mods(self, l: int, j: int):
+        """(gate, shift, scale) of sub-layer j of block l (model.py:317-336, 375)."""
+        mod, s = self.mod, self.s
+        if j < 2:
+            return mod[l, j, 2], mod[l, j + 1, 0], mod[l, j + 1, 1]
+        if l + 1 < s.layers:
+            return mod[l, 2, 2], mod[l + 1, 0, 0], mod[l + 1, 0, 1]
+        shift, scale = self.fin.chunk(2, dim=-1)
+        return mod[-1, 2, 2], shift, scale + 1
+
+    def run(self):
+        """One forward's op sequence (model.py:366-375 or :434-472)."""
+        afb, s, mod, op = self.afb, self.s, self.mod, self._op
+        H = s.heads
+        with torch.no_grad():
+            if not self.fp8:
+                op("adaln", afb.adaln, self.z0, mod[0, 0, 0], mod[0, 0, 1])
+                for l in range(s.layers):
+                    op("qkv_norm_rope", afb.qkv_norm_rope, self.qkv[l], self.qw[l], self.kw[l],
+                       self.cos, self.sin, H)
+                    op("residual_adaln", afb.residual_adaln, self.sub[l][0], self.res[l][0],
+                       *self.block_mods(l, 0))
+                    op("head_norm", afb.head_norm, self.xq[l], self.xw[l], H)
+                    op("residual_adaln", afb.residual_adaln, self.sub[l][1], self.res[l][1],
+                       *self.block_mods(l, 1))
+                    if l + 1 < s.layers:
+                        op("residual_adaln", afb.residual_adaln, self.sub[l][2], self.res[l][2],
+                           *self.block_mods(l, 2))
+            else:
+                op("adaln_fp8", afb.adaln_fp8, self.z0, mod[0, 0, 0], mod[0, 0, 1])
+                for l in range(s.layers):
+                    op("qkv_norm_rope", afb.qkv_norm_rope, self.qkv[l], self.qw[l], self.kw[l],
+                       self.cos, self.sin, H)
+                    op("rowquant", afb.rowquant, self.attn[l][0])
+                    op("residual_adaln_fp8", afb.residual_adaln_fp8, self.sub[l][0], self.res[l][0],
+                       *self.block_mods(l, 0))
+                    op("head_norm", afb.head_norm, self.xq[l], self.xw[l], H)
+                    op("rowquant", afb.rowquant, self.attn[l][1])
+                    op("residual_adaln_fp8", afb.residual_adaln_fp8, self.sub[l][1], self.res[l][1],
+                       *self.block_mods(l, 1))
+                    op("rowquant_gelu", afb.rowquant, self.up[l], gelu=True)
+                    if l + 1 < s.layers:
+                        op("residual_adaln_fp8", afb.residual_adaln_fp8, self.sub[l][2],
+                           self.res[l][2], *self.block_mods(l, 2))
+            L = s.layers - 1
+            op("residual_adaln", afb.residual_adaln, self.sub[L][2], self.res[L][2],
+               *self.block_mods(L, 2))
+
+
+def capture(step: Step):
+    """CUDA graph of one step (its outputs live in the graph's memory pool)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step.run()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step.run()
+    torch.cuda.synchronize()
+    return g
+
+
+def instrumented_capture(step: Step):
+    """A copy of the step graph with external events around every residual_adaln."""
+    events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+    pending: list[torch.cuda.Event] = []
+
+    def hook(before: bool):
+        if before:
+            ev = torch.cuda.Event(enable_timing=True, external=True)
+            ev.record()
+            pending.append(ev)
+        else:
+            ev = torch.cuda.Event(enable_timing=True, external=True)
+            ev.record()
+            events.append((pending.pop(), ev))
+
+    from anima_flat_b200 import _lib
+
+    step.timed_hook = hook
+    pdl = _lib.load().afb_get_pdl()
+    _lib.set_pdl(False)  # time each launch on its own, without overlap
+    try:
+        g = capture(step)
+    finally:
+        step.timed_hook = None
+        _lib.set_pdl(bool(pdl))
+    # events from the warm-up runs inside capture() are discarded
+    return g, events[-step.calls.count(step.timed):]
+
+
+# ------------------------------------------------------------ our arm --
+def run_ours(args, world, rank, local):
+    import anima_flat_b200 as afb
+    from anima_flat_b200 import _lib
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    _lib.set_pdl(not args.no_pdl)
+    shape = W.Shape(batch=2 if args.workload == "cfg3" else 1)
+    step = Step(shape, fp8=args.workload == "cfg3", device=device, seed=1234 + rank)
+    n_launch = len(step.calls)
+
+    g = capture(step)
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        g.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_local = t0.elapsed_time(t1)
+    clocks = sampler.stop()
+
+    ms = ms_local
+    if world > 1:
+        t = torch.tensor([ms_local], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    total_bytes = step.bytes * world * args.steps
+    value = total_bytes / (ms * 1e-3) / 1e9
+    rows_total = shape.rows * world * args.steps
+    del g
+
+    # --- dominant kernel, per launch (instrumented graph, same K) ----------
+    dominant = step.timed
+    g2, evs = instrumented_capture(step)
+    per_launch = []
+    for _ in range(max(3, args.warmup)):
+        g2.replay()
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        g2.replay()
+        torch.cuda.synchronize()
+        per_launch += [a.elapsed_time(b) for a, b in evs]
+    del g2
+    avg_ms = sum(per_launch) / len(per_launch)
+    dom_bytes = W.call_bytes(dominant, shape)
+    achieved = dom_bytes / (avg_ms * 1e-3) / 1e9
+    peak, peak_src = peak_hbm()
+    traffic = ncu_traffic(f"{dominant}_{args.workload}")
+
+    # --- end to end through the public API with host buffers --------------
+    e2e = run_e2e(step, shape, args, world, device, barrier)
+
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.1) modulation; no dataset needed)",
+        "config": {
+            "workload": ("cfg2: Cosmos-Predict2-2B BF16 forward fused-op sequence (forward_fused), "
+                         "1024x1024, 28 blocks, 141 launches")
+            if not step.fp8 else
+            ("cfg3: Cosmos-Predict2-2B FP8 forward fused-op sequence (forward_fp8) with CFG batch 2, "
+             f"{n_launch} launches"),
+            "global_batch": shape.batch * world,
+            "seq_len": shape.seq,
+            "rows_per_gpu": shape.rows,
+            "dim": shape.dim,
+            "heads": shape.heads,
+            "head_dim": shape.head_dim,
+            "parallelism": f"rows sharded by sequence over {world} GPU(s); no collective on the hot path",
+            "l2": "inputs larger than L2: every call reads distinct buffers "
+                  f"({step.bytes / 1e9:.2f} GB of algorithmic traffic per step)",
+            "cuda_graph": True,
+            "pdl": not args.no_pdl,
+        },
+        "mrows_per_s": round(rows_total / (ms * 1e-3) / 1e6, 3),
+        "pct_of_hbm_peak": round(100.0 * value / world / peak, 1),
+        "pct_of_spec_8tbs": round(100.0 * value / world / 8000.0, 1),
+        "gpu_launches": n_launch * args.steps,
+        "roofline": {
+            "kernel": f"{dominant} (adaln_fwd_kernel)",
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "peak_source": peak_src,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "traffic": traffic,
+            "bytes_per_launch": dom_bytes,
+            "avg_launch_us": round(avg_ms * 1e3, 3),
+            "launches_timed": len(per_launch),
+        },
+        "clocks": clocks,
+        "e2e": e2e,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(step: Step, shape: W.Shape, args, world, device, barrier) -> dict:
+    """The same op sequence through the public API with host buffers: each
+    call's fresh inputs are copied from pinned host memory, each output is
+    copied back to pinned host memory, all inside the timed region."""
+    afb = step.afb
+    s = shape
+    H = s.heads
+    B, S, D = s.batch, s.seq, s.dim
+    pin = lambda *d: torch.empty(*d, dtype=torch.bfloat16).pin_memory()
+    h_qkv, h_act = pin(B, S, 3 * D), pin(B, S, D)
+    h_act.copy_(step.sub[0][0].cpu())
+    h_qkv.copy_(step.qkv[0].cpu())
+    h_out = pin(B, S, D)
+    d_qkv = torch.empty(B, S, 3 * D, dtype=torch.bfloat16, device=device)
+    d_x = torch.empty(B, S, D, dtype=torch.bfloat16, device=device)
+    nbytes = lambda t: t.numel() * t.element_size()
+
+    def run_once():
+        h2d = d2h = 0
+        mod = step.mod
+        with torch.no_grad():
+            d_x.copy_(h_act, non_blocking=True)
+            h2d += nbytes(h_act)
+            z = d_x.clone()
+            hid = afb.adaln(z, mod[0, 0, 0], mod[0, 0, 1])
+            h_out.copy_(hid, non_blocking=True)
+            d2h += nbytes(hid)
+            for l in range(s.layers):
+                d_qkv.copy_(h_qkv, non_blocking=True)
+                h2d += nbytes(h_qkv)
+                q, k, _ = afb.qkv_norm_rope(d_qkv, step.qw[l], step.kw[l], step.cos, step.sin, H)
+                h_out.copy_(q.view(B, S, D), non_blocking=True)
+                h_out.copy_(k.view(B, S, D), non_blocking=True)
+                d2h += nbytes(q) + nbytes(k)
+                for j in range(3):
+                    if j == 1:
+                        d_x.copy_(h_act, non_blocking=True)
+                        h2d += nbytes(h_act)
+                        y = afb.head_norm(d_x, step.xw[l], H)
+                        h_out.copy_(y.view(B, S, D), non_blocking=True)
+                        d2h += nbytes(y)
+                    d_x.copy_(h_act, non_blocking=True)
+                    h2d += nbytes(h_act)
+                    hid, z = afb.residual_adaln(d_x, z, *step.block_mods(l, j))
+                    h_out.copy_(hid, non_blocking=True)
+                    d2h += nbytes(hid)
+            h_out.copy_(z, non_blocking=True)
+            d2h += nbytes(z)
+        return h2d, d2h
+
+    for _ in range(2):
+        run_once()
+    torch.cuda.synchronize()
+    n = max(1, min(args.steps, args.e2e_steps))
+    barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        h2d, d2h = run_once()
+    b.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    calls = W.bf16_forward_calls(s)
+    val = W.step_bytes(calls, s) * world * n / (ms * 1e-3) / 1e9
+    return {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms / n, 3),
+            "path": "anima_flat_b200 public API (torch custom ops -> C ABI), pinned host buffers, "
+                    "one stream, copies and kernels serialised"}
+
+
+# -------------------------------------------------- CPU baseline / reference --
+def cpu_sequence(shape: W.Shape, seed: int = 0):
+    """The reference's unfused torch fp32 eager composition of the step's ops
+    on the host cores (oracle/formulation.py)."""
+    from oracle import formulation as Fm
+
+    from anima_flat_b200.tables import rope_tables
+
+    s = shape
+    g = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    act = lambda *d: torch.randn(*d, generator=g).to(bf)
+    B, S, D, H, hd = s.batch, s.seq, s.dim, s.heads, s.head_dim
+    side = int(round(S ** 0.5))
+    cos, sin = rope_tables(side, S // side, hd, "cpu", (4.0, 4.0))
+    mod = (torch.randn(3, 3, B, D, generator=g) * 0.1).to(bf)
+    mod[:, 1] += 1.0
+    w = 1.0 + 0.02 * torch.randn(hd, generator=g)
+    z0, qkv, x, xq = act(B, S, D), act(B, S, 3 * D), act(B, S, D), act(B, S, D)
+
+    def run():
+        z = z0
+        Fm.adaln(z, mod[0, 0], mod[0, 1])
+        for l in range(s.layers):
+            Fm.qkv_norm_rope(qkv, w, w, cos, sin, H)
+            _, z = Fm.residual_adaln(x, z, mod[0, 2], mod[1, 0], mod[1, 1])
+            Fm.head_norm(xq, w, H)
+            _, z = Fm.residual_adaln(x, z, mod[1, 2], mod[2, 0], mod[2, 1])
+            _, z = Fm.residual_adaln(x, z, mod[2, 2], mod[0, 0], mod[0, 1])
+
+    return run, W.step_bytes(W.bf16_forward_calls(s), s)
+
+
+def cpu_baseline(budget_s: float = 12.0) -> dict:
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    shape = W.Shape(seq=256)
+    run, nbytes = cpu_sequence(shape)
+    run()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 1000:
+            break
+    return {"value": round(nbytes * n / el / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": (f"{n} steps of the config-2 op sequence (141 ops) on config-1 shapes "
+                       "(B=1, S=256, D=2048, 16x128 heads), torch fp32 eager composition "
+                       "(oracle/formulation.py), same byte model"),
+            "seconds": round(el, 2)}
+
+
+def run_reference(args, world, rank):
+    """The reference arm: the unfused PyTorch-eager fp32 composition the task
+    names as the reference's CPU path (the reference ships no CPU kernels),
+    on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    shape = W.Shape(seq=256)
+    run, nbytes = cpu_sequence(shape)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    el = time.perf_counter() - t0
+    value = nbytes * args.steps / el / 1e9
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(el * 1e3 / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "cfg2 op sequence (141 ops) on a bounded CPU sample: config-1 "
+                               "shapes B=1, S=256, D=2048, 16x128 heads",
+                   "global_batch": 1, "seq_len": 256, "parallelism": "host threads"},
+        "mrows_per_s": round(shape.rows * args.steps / el / 1e6, 4),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port",
+                         "sample": "torch fp32 eager composition of the reference's formulas "
+                                   "(oracle/formulation.py), config-1 shapes"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_info()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,120 @@
+/*
+ * anima_flat_b200 — C ABI of the fused DiT layer ops for NVIDIA B200 (sm_100a).
+ *
+ * Each entry point replaces one Triton kernel launch of the reference
+ * (tan0210/anima-flat, src/kernels/*.py) and takes what that launch takes:
+ * raw device pointers, sizes, eps and the CUDA stream to launch on (a
+ * cudaStream_t passed as void*; NULL is the legacy default stream).  All
+ * launches are asynchronous on that stream; nothing allocates.
+ *
+ * Types.  Activations, modulation vectors (gate, shift, scale) and the
+ * weight gradients of the modulation vectors are bf16 (uint16 bit patterns);
+ * RMSNorm weights, RoPE tables, FP8 row scales and norm-weight gradients are
+ * fp32; FP8 codes are OCP e4m3 "fn" bytes (max 448), the layout torch calls
+ * float8_e4m3fn.  Every tensor is dense row-major; bf16 tensors must be
+ * 16-byte aligned.  `scale` already includes the +1 (reference model.py:228).
+ *
+ * Errors.  Return 0 on success, otherwise a cudaError_t value
+ * (cudaErrorInvalidValue = 1 for rejected arguments); afb_last_error()
+ * returns this thread's message for the last failure.
+ */
+#ifndef ANIMA_FLAT_B200_H_
+#define ANIMA_FLAT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ABI revision of this header. */
+int afb_abi_version(void);
+
+/* Message of this thread's last failed call ("" if none). */
+const char* afb_last_error(void);
+void afb_clear_error(void);
+
+/* Programmatic dependent launch on (1, default) or off (0).  Also read from
+ * the environment variable AFB_PDL=0 at first use. */
+void afb_set_pdl(int enabled);
+int afb_get_pdl(void);
+
+/* ----------------------------------------------------------------------- */
+/* AdaLN modulate                                                           */
+/* ----------------------------------------------------------------------- */
+
+/* Gated residual + affine-free LayerNorm + modulate.
+ * Replaces src/kernels/adaln.py:49-75 (anima_flat::residual_adaln launching
+ * _residual_adaln_kernel, adaln.py:10-46, HAS_X=True).
+ *   z = bf16(residual + bf16(gate * x));  h = bf16(LN(z) * scale + shift)
+ * x, residual, h, z: [batch, seq, dim]; gate, shift, scale: [batch, dim]. */
+int afb_residual_adaln(const void* x, const void* residual, const void* gate,
+                       const void* shift, const void* scale, void* h, void* z,
+                       int64_t batch, int64_t seq, int64_t dim, float eps,
+                       void* stream);
+
+/* LayerNorm + modulate without the residual.
+ * Replaces src/kernels/adaln.py:83-103 (anima_flat::adaln, HAS_X=False). */
+int afb_adaln(const void* z, const void* shift, const void* scale, void* h,
+              int64_t batch, int64_t seq, int64_t dim, float eps, void* stream);
+
+/* residual_adaln with the modulated output quantised to FP8 per row.
+ * Replaces src/kernels/fp8.py:100-128 (anima_flat::residual_adaln_fp8
+ * launching _residual_adaln_fp8_kernel, fp8.py:56-97, HAS_X=True).
+ * q: [batch*seq, dim] e4m3; s: [batch*seq] fp32; z as above. */
+int afb_residual_adaln_fp8(const void* x, const void* residual, const void* gate,
+                           const void* shift, const void* scale, void* q, void* s,
+                           void* z, int64_t batch, int64_t seq, int64_t dim,
+                           float eps, void* stream);
+
+/* adaln with FP8 output.  Replaces src/kernels/fp8.py:141-163
+ * (anima_flat::adaln_fp8, HAS_X=False). */
+int afb_adaln_fp8(const void* z, const void* shift, const void* scale, void* q,
+                  void* s, int64_t batch, int64_t seq, int64_t dim, float eps,
+                  void* stream);
+
+/* ----------------------------------------------------------------------- */
+/* FP8 row quantisation                                                     */
+/* ----------------------------------------------------------------------- */
+
+/* Per-row e4m3 quantisation, optionally after the A&S 7.1.26 GELU.
+ * Replaces src/kernels/fp8.py:295-301 (anima_flat::rowquant launching
+ * _rowquant_kernel, fp8.py:273-292).  x: [rows, K] bf16, K a multiple of 16
+ * up to 16384; q: [rows, K] e4m3; s: [rows] fp32. */
+int afb_rowquant(const void* x, void* q, void* s, int64_t rows, int64_t K, int gelu,
+                 void* stream);
+
+/* Test hook: fast and canonical GELU of n bf16 values (fp32 outputs).  The
+ * GELU row quantisation relies on the bound between the two.  No reference
+ * counterpart. */
+int afb_gelu_probe(const void* x, void* fast, void* canon, int64_t n, void* stream);
+
+/* ----------------------------------------------------------------------- */
+/* q/k RMSNorm + 3D RoPE, head norm                                          */
+/* ----------------------------------------------------------------------- */
+
+/* Replaces src/kernels/rope.py:175-193 (anima_flat::qkv_norm_rope) and, with
+ * v != NULL, rope.py:504-523 (anima_flat::qkv_norm_rope_v), both launching
+ * _qkv_norm_rope_kernel (rope.py:61-143).
+ * qkv: [batch, seq, 3*heads*head_dim] (q | k | v); q_weight, k_weight:
+ * [head_dim] fp32; cos, sin: [seq, head_dim/2] fp32; q, k, v:
+ * [batch, seq, heads, head_dim].  head_dim is 64, 128 or 256. */
+int afb_qkv_norm_rope(const void* qkv, const void* q_weight, const void* k_weight,
+                      const void* cos, const void* sin, void* q, void* k, void* v,
+                      int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
+                      float eps, void* stream);
+
+/* Per-head RMSNorm without rotation (cross-attention queries).
+ * Replaces src/kernels/rope.py:203-212 (anima_flat::head_norm launching
+ * _head_norm_kernel, rope.py:146-172).  x: [batch, seq, heads*head_dim];
+ * weight: [head_dim] fp32; y: [batch, seq, heads, head_dim]. */
+int afb_head_norm(const void* x, const void* weight, void* y, int64_t batch,
+                  int64_t seq, int64_t heads, int64_t head_dim, float eps,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANIMA_FLAT_B200_H_ */

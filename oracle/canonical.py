@@ -1,0 +1,135 @@
+"""numpy front end of oracle.c (TEST INFRASTRUCTURE ONLY; see oracle/__init__.py).
+
+Arrays: bf16 tensors are passed as uint16 bit patterns, e4m3 as uint8.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_float, c_int, c_int64, c_void_p
+
+import numpy as np
+
+from .build import build
+
+RNE = 0
+INTERP = 1
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        L = ctypes.CDLL(str(build()))
+        P, I, F, N = c_void_p, c_int64, c_float, c_int
+        sigs = {
+            "orc_adaln_fwd": ([P] * 9 + [I, I, I, F, N, N, N], None),
+            "orc_rowquant": ([P, P, P, P, I, I, N, N], None),
+            "orc_qkv_norm_rope": ([P] * 8 + [I, I, I, I, F, N], None),
+            "orc_head_norm": ([P, P, P, I, I, I, I, F, N], None),
+            "orc_gelu_many": ([P, P, I], None),
+            "orc_canonical_sum": ([P, I, N], c_float),
+            "orc_numpy_sum": ([P, I], c_float),
+            "orc_f32_to_e4m3": ([c_float, N], ctypes.c_uint8),
+            "orc_e4m3_to_f32": ([ctypes.c_uint8], c_float),
+        }
+        for name, (args, res) in sigs.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags.c_contiguous
+    return a.ctypes.data_as(c_void_p)
+
+
+def u16(a) -> np.ndarray:
+    """Contiguous uint16 view/copy of a bf16 bit-pattern array."""
+    return np.ascontiguousarray(a, dtype=np.uint16)
+
+
+def f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def bf16_bits_to_f32(a: np.ndarray) -> np.ndarray:
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+def e4m3_to_f32(a: np.ndarray) -> np.ndarray:
+    table = np.array([lib().orc_e4m3_to_f32(i) for i in range(256)], dtype=np.float32)
+    return table[a]
+
+
+def canonical_sum(x: np.ndarray, P: int = 32) -> float:
+    x = f32(x)
+    return lib().orc_canonical_sum(_p(x), x.size, P)
+
+
+def numpy_sum(x: np.ndarray) -> float:
+    x = f32(x)
+    return lib().orc_numpy_sum(_p(x), x.size)
+
+
+def adaln_fwd(res, shift, scale, x=None, gate=None, eps=1e-6, fp8=False, mode=RNE):
+    """Row AdaLN (optionally gated residual, optionally FP8).  res/x: [B, S, D] uint16."""
+    res = u16(res)
+    B, S, D = res.shape
+    shift, scale = u16(shift), u16(scale)
+    has_x = x is not None
+    x = u16(x) if has_x else None
+    gate = u16(gate) if has_x else None
+    h = None if fp8 else np.empty((B, S, D), np.uint16)
+    z = np.empty((B, S, D), np.uint16) if has_x else None
+    q = np.empty((B, S, D), np.uint8) if fp8 else None
+    s = np.empty((B * S, 1), np.float32) if fp8 else None
+    lib().orc_adaln_fwd(_p(x), _p(res), _p(gate), _p(shift), _p(scale), _p(h), _p(z), _p(q),
+                        _p(s), B, S, D, eps, int(has_x), int(fp8), mode)
+    return {"h": h, "z": z, "q": q, "s": s}
+
+
+def rowquant(x, gelu=False, mode=RNE, want_y=False):
+    """Per-row e4m3 quantisation.  x: [..., K] uint16 -> (q uint8, s [rows,1] f32[, y])."""
+    x = u16(x)
+    K = x.shape[-1]
+    rows = x.size // K
+    q = np.empty(x.shape, np.uint8)
+    s = np.empty((rows, 1), np.float32)
+    y = np.empty(x.shape, np.float32) if want_y else None
+    lib().orc_rowquant(_p(x), _p(q), _p(s), _p(y), rows, K, int(gelu), mode)
+    return (q, s, y) if want_y else (q, s)
+
+
+def qkv_norm_rope(qkv, qw, kw, cos, sin, heads, eps=1e-5, with_v=False, mode=RNE):
+    qkv = u16(qkv)
+    B, S, W = qkv.shape
+    hd = W // (3 * heads)
+    q = np.empty((B, S, heads, hd), np.uint16)
+    k = np.empty_like(q)
+    v = np.empty_like(q) if with_v else None
+    lib().orc_qkv_norm_rope(_p(qkv), _p(f32(qw)), _p(f32(kw)), _p(f32(cos)), _p(f32(sin)), _p(q),
+                            _p(k), _p(v), B, S, heads, hd, eps, mode)
+    return q, k, v
+
+
+def head_norm(x, w, heads, eps=1e-5, mode=RNE):
+    x = u16(x)
+    B, S, W = x.shape
+    hd = W // heads
+    y = np.empty((B, S, heads, hd), np.uint16)
+    lib().orc_head_norm(_p(x), _p(f32(w)), _p(y), B, S, heads, hd, eps, mode)
+    return y
+
+
+def gelu(x_bits: np.ndarray) -> np.ndarray:
+    """Canonical GELU of bf16 inputs (fp32 outputs)."""
+    x = u16(x_bits)
+    y = np.empty(x.shape, np.float32)
+    lib().orc_gelu_many(_p(x), _p(y), x.size)
+    return y

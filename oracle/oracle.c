@@ -1,0 +1,346 @@
+/*
+ * CPU oracle for the fused DiT layer ops — TEST INFRASTRUCTURE ONLY.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load
+ * this file's library; the product path (anima_flat_b200) never does.
+ *
+ * It restates the reference's per-row formulas (tan0210/anima-flat,
+ * src/kernels/adaln.py, fp8.py, rope.py; cited per function) in plain C with
+ * IEEE-754 binary32 arithmetic: compiled with -ffp-contract=off and without
+ * -ffast-math, every + - * / sqrtf is one correctly rounded operation and
+ * fmaf is used only where written.  Reductions follow the canonical order
+ * (canonical_sum below), which fixes the association the reference leaves to
+ * Triton's autotuned num_warps.  bf16 rounding is round-to-nearest-even;
+ * e4m3 ("fn", max 448) rounding is round-to-nearest-even with saturation.
+ *
+ * ROUND_INTERP reproduces Triton's CPU interpreter instead
+ * (triton/runtime/interpreter.py): bf16 casts truncate, the e4m3 cast is the
+ * interpreter's (e4m3_interp), tl.sum is numpy's pairwise float32 sum
+ * (numpy_sum), and GELU uses separate multiply/add and libm expf.  In that
+ * mode the oracle can be compared with golden vectors produced by running the
+ * reference's own Triton kernels under TRITON_INTERPRET=1.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define ROUND_RNE 0
+#define ROUND_INTERP 1
+
+/* ---------------------------------------------------------------- bits -- */
+
+static float f_from_bits(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static uint32_t bits_from_f(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+float orc_bf16_to_f32(uint16_t h) { return f_from_bits((uint32_t)h << 16); }
+
+uint16_t orc_f32_to_bf16(float f, int mode) {
+  uint32_t u = bits_from_f(f);
+  if (isnan(f)) return (uint16_t)(((u >> 16) & 0x8000u) | 0x7fc0u);
+  if (mode == ROUND_INTERP) return (uint16_t)(u >> 16);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+static float rbf(float f, int mode) { return orc_bf16_to_f32(orc_f32_to_bf16(f, mode)); }
+
+/* The interpreter's fp32 -> e4m3 cast (interpreter.py _convert_float with
+ * RTNE): keep 3 mantissa bits, add the first dropped bit, OR the (possibly
+ * carried) mantissa into the exponent field.  Outputs below 2^-9 are not
+ * modelled (returned as signed zero); callers compare them loosely. */
+static uint8_t e4m3_interp(float f) {
+  const uint32_t u = bits_from_f(f), sign = u >> 31, e = (u >> 23) & 0xffu, sig = u & 0x7fffffu;
+  if (e == 0 && sig == 0) return (uint8_t)(sign << 7);
+  int eo = (int)e - 127 + 7;
+  if (eo < 0) eo = 0;
+  if (eo > 15) eo = 15;
+  uint32_t so = ((sig >> 20) & 7u) + ((sig & (1u << 19)) ? 1u : 0u);
+  if (eo == 0) {
+    const int shift = 121 - (int)e;
+    so = (shift >= 1 && shift <= 3) ? ((so >> shift) | (1u << (3 - shift))) : 0u;
+  }
+  return (uint8_t)((sign << 7) | ((uint32_t)eo << 3) | so);
+}
+
+/* e4m3fn: 1 sign, 4 exponent (bias 7), 3 mantissa bits; 0x7f is NaN, max
+ * finite 448 = 1.75 * 2^8, subnormals are multiples of 2^-9. */
+uint8_t orc_f32_to_e4m3(float f, int mode) {
+  if (mode == ROUND_INTERP) return e4m3_interp(f);
+  if (isnan(f)) return 0x7f;
+  const uint8_t sign = signbit(f) ? 0x80 : 0x00;
+  float a = fabsf(f);
+  if (a >= 448.0f) return sign | 0x7e;
+  int e2;
+  (void)frexpf(a, &e2); /* a in [2^(e2-1), 2^e2) */
+  int E = e2 - 1;
+  if (a == 0.0f || E < -6) { /* subnormal grid, step 2^-9 */
+    float r = nearbyintf(a * 512.0f); /* a * 512 is exact */
+    return sign | (uint8_t)r; /* r == 8 encodes 2^-6, the smallest normal */
+  }
+  float r = nearbyintf(ldexpf(a, 3 - E)); /* argument in [8, 16), exact */
+  if (r == 16.0f) { r = 8.0f; E += 1; }
+  if (E > 8 || (E == 8 && r > 14.0f)) return sign | 0x7e; /* satfinite */
+  return sign | (uint8_t)(((E + 7) << 3) | ((int)r - 8));
+}
+
+float orc_e4m3_to_f32(uint8_t b) {
+  const float sign = (b & 0x80) ? -1.0f : 1.0f;
+  const int E = (b >> 3) & 0xf, m = b & 7;
+  if (E == 0xf && m == 7) return NAN;
+  if (E == 0) return sign * ldexpf((float)m, -9);
+  return sign * ldexpf((float)(8 + m), E - 10);
+}
+
+/* -------------------------------------------------------- canonical sum -- */
+
+/* Sum of x[0..n) (n a multiple of 8) in the canonical order: zero-pad to
+ * NVp = max(P, pow2ceil(n/8)) vectors of 8; halve the vector count by adding
+ * vector v + NVp/2 into vector v until P remain; reduce each remaining vector
+ * as ((x0+x1)+(x2+x3))+((x4+x5)+(x6+x7)); halve the P partials the same way. */
+float orc_canonical_sum(const float* x, int64_t n, int P) {
+  int64_t nv = n / 8, nvp = P;
+  while (nvp < nv) nvp <<= 1;
+  float* X = (float*)calloc((size_t)(nvp * 8), sizeof(float));
+  memcpy(X, x, (size_t)n * sizeof(float));
+  while (nvp > P) {
+    const int64_t half = nvp / 2;
+    for (int64_t v = 0; v < half; ++v)
+      for (int k = 0; k < 8; ++k) X[v * 8 + k] = X[v * 8 + k] + X[(v + half) * 8 + k];
+    nvp = half;
+  }
+  float* p = (float*)malloc((size_t)P * sizeof(float));
+  for (int v = 0; v < P; ++v) {
+    const float* q = X + (int64_t)v * 8;
+    p[v] = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
+  }
+  for (int w = P; w > 1; w /= 2)
+    for (int v = 0; v < w / 2; ++v) p[v] = p[v] + p[v + w / 2];
+  const float r = p[0];
+  free(p);
+  free(X);
+  return r;
+}
+
+/* numpy's float32 add.reduce order (pairwise with 8 accumulators, blocks of
+ * 128), the order tl.sum takes under the Triton interpreter. */
+float orc_numpy_sum(const float* a, int64_t n) {
+  if (n < 8) {
+    float r = 0.0f;
+    for (int64_t i = 0; i < n; ++i) r = r + a[i];
+    return r;
+  }
+  if (n <= 128) {
+    float r[8];
+    for (int j = 0; j < 8; ++j) r[j] = a[j];
+    int64_t i = 8;
+    for (; i < n - (n % 8); i += 8)
+      for (int j = 0; j < 8; ++j) r[j] = r[j] + a[i + j];
+    float res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+    for (; i < n; ++i) res = res + a[i];
+    return res;
+  }
+  int64_t n2 = n / 2;
+  n2 -= n2 % 8;
+  return orc_numpy_sum(a, n2) + orc_numpy_sum(a + n2, n - n2);
+}
+
+static float row_sum(const float* x, int64_t n, int P, int mode) {
+  return (mode == ROUND_INTERP) ? orc_numpy_sum(x, n) : orc_canonical_sum(x, n, P);
+}
+
+/* --------------------------------------------------------------- AdaLN -- */
+
+/* src/kernels/adaln.py:26-46 (bf16 output) and src/kernels/fp8.py:73-97 (FP8
+ * output).  One row of D: z = bf16(res + bf16(gate*x)) (has_x) or z = res;
+ * mean, rstd of z; y = (d*rstd)*scale + shift; h = bf16(y) or
+ * s = max(max|y|, 1e-12)/448, q = e4m3(clamp(y/s, +-448)). */
+void orc_adaln_fwd(const uint16_t* x, const uint16_t* res, const uint16_t* gate,
+                   const uint16_t* shift, const uint16_t* scale, uint16_t* h, uint16_t* z,
+                   uint8_t* q, float* s, int64_t B, int64_t S, int64_t D, float eps, int has_x,
+                   int fp8, int mode) {
+  float* zf = (float*)malloc((size_t)D * sizeof(float));
+  float* t = (float*)malloc((size_t)D * sizeof(float));
+  float* y = (float*)malloc((size_t)D * sizeof(float));
+  for (int64_t row = 0; row < B * S; ++row) {
+    const int64_t b = row / S, o = row * D, po = b * D;
+    for (int64_t i = 0; i < D; ++i) {
+      const float r = orc_bf16_to_f32(res[o + i]);
+      if (has_x) {
+        const float p = rbf(orc_bf16_to_f32(gate[po + i]) * orc_bf16_to_f32(x[o + i]), mode);
+        const uint16_t zb = orc_f32_to_bf16(r + p, mode);
+        if (z) z[o + i] = zb;
+        zf[i] = orc_bf16_to_f32(zb);
+      } else {
+        zf[i] = r;
+      }
+    }
+    const float mean = row_sum(zf, D, 32, mode) / (float)D;
+    for (int64_t i = 0; i < D; ++i) {
+      const float d = zf[i] - mean;
+      t[i] = d * d;
+    }
+    const float var = row_sum(t, D, 32, mode) / (float)D;
+    const float rstd = 1.0f / sqrtf(var + eps);
+    float amax = 0.0f;
+    for (int64_t i = 0; i < D; ++i) {
+      const float d = zf[i] - mean;
+      y[i] = ((d * rstd) * orc_bf16_to_f32(scale[po + i])) + orc_bf16_to_f32(shift[po + i]);
+      amax = fmaxf(amax, fabsf(y[i]));
+    }
+    if (!fp8) {
+      for (int64_t i = 0; i < D; ++i) h[o + i] = orc_f32_to_bf16(y[i], mode);
+    } else {
+      const float sc = fmaxf(amax, 1e-12f) / 448.0f;
+      s[row] = sc;
+      for (int64_t i = 0; i < D; ++i)
+        q[o + i] = orc_f32_to_e4m3(fminf(fmaxf(y[i] / sc, -448.0f), 448.0f), mode);
+    }
+  }
+  free(zf);
+  free(t);
+  free(y);
+}
+
+/* ---------------------------------------------------------------- GELU -- */
+
+/* exp(a), a <= 0: Cody-Waite reduction a = k ln2 + r (ln2 split in two parts),
+ * degree-7 Taylor polynomial of exp(r) in Horner form with fmaf, times 2^k;
+ * results below 2^-126 are scaled in two exact steps so that only the last
+ * multiplication rounds. */
+float orc_exp_nonpos(float a) {
+  if (a < -104.0f) return 0.0f;
+  const float k = rintf(a * 1.44269502162933349609375f);
+  float r = fmaf(k, -0.693145751953125f, a);
+  r = fmaf(k, -1.428606765330187e-06f, r);
+  float p = 1.98412701138295233249664306640625e-04f; /* 1/7! */
+  p = fmaf(p, r, 1.38888892251998186111450195312500e-03f); /* 1/6! */
+  p = fmaf(p, r, 8.33333376795053482055664062500000e-03f); /* 1/5! */
+  p = fmaf(p, r, 4.16666679084300994873046875000000e-02f); /* 1/4! */
+  p = fmaf(p, r, 1.66666671633720397949218750000000e-01f); /* 1/3! */
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const int ki = (int)k;
+  if (ki >= -125) return p * ldexpf(1.0f, ki);
+  return (p * ldexpf(1.0f, ki + 64)) * ldexpf(1.0f, -64);
+}
+
+/* GELU with the Abramowitz & Stegun 7.1.26 erf (src/kernels/fp8.py:260-270),
+ * Horner steps as fmaf. */
+float orc_gelu(float x) {
+  const float z = x * 0.707106769084930419921875f;
+  const float az = fabsf(z);
+  const float t = 1.0f / (1.0f + 0.3275911f * az);
+  float p = fmaf(1.061405429f, t, -1.453152027f);
+  p = fmaf(p, t, 1.421413741f);
+  p = fmaf(p, t, -0.284496736f);
+  p = fmaf(p, t, 0.254829592f);
+  p = p * t;
+  const float e = orc_exp_nonpos(-(az * az));
+  const float yv = fmaf(-p, e, 1.0f);
+  const float erf = (z < 0.0f) ? -yv : yv;
+  return (0.5f * x) * (1.0f + erf);
+}
+
+/* The same formula as the interpreter evaluates it: no fused multiply-add,
+ * libm expf (the interpreter calls numpy's exp, which may differ in the last
+ * bit). */
+static float gelu_interp(float x) {
+  const float z = x * 0.707106769084930419921875f;
+  const float az = fabsf(z);
+  const float t = 1.0f / (1.0f + 0.3275911f * az);
+  const float p =
+      ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
+       0.254829592f) * t;
+  const float yv = 1.0f - p * expf(-az * az);
+  return 0.5f * x * (1.0f + ((z < 0.0f) ? -yv : yv));
+}
+
+static float gelu_mode(float x, int mode) { return mode == ROUND_INTERP ? gelu_interp(x) : orc_gelu(x); }
+
+void orc_gelu_many(const uint16_t* x, float* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = orc_gelu(orc_bf16_to_f32(x[i]));
+}
+
+/* src/kernels/fp8.py:283-292: y = gelu(x) or x; s = max(max|y|,1e-12)/448;
+ * q = e4m3(clamp(y/s, +-448)).  `y_out` (optional) receives y. */
+void orc_rowquant(const uint16_t* x, uint8_t* q, float* s, float* y_out, int64_t rows, int64_t K,
+                  int gelu, int mode) {
+  float* y = (float*)malloc((size_t)K * sizeof(float));
+  for (int64_t row = 0; row < rows; ++row) {
+    float amax = 0.0f;
+    for (int64_t i = 0; i < K; ++i) {
+      const float v = orc_bf16_to_f32(x[row * K + i]);
+      y[i] = gelu ? gelu_mode(v, mode) : v;
+      amax = fmaxf(amax, fabsf(y[i]));
+    }
+    const float sc = fmaxf(amax, 1e-12f) / 448.0f;
+    s[row] = sc;
+    for (int64_t i = 0; i < K; ++i) {
+      q[row * K + i] = orc_f32_to_e4m3(fminf(fmaxf(y[i] / sc, -448.0f), 448.0f), mode);
+      if (y_out) y_out[row * K + i] = y[i];
+    }
+  }
+  free(y);
+}
+
+/* -------------------------------------------------- q/k RMSNorm + RoPE -- */
+
+/* One head (src/kernels/rope.py:39-58): rstd over hd dims (canonical sum with
+ * P = hd/8 partials), a/b = bf16((x*rstd)*w), then optionally
+ * a' = a*cos - b*sin, b' = b*cos + a*sin. */
+static void head_fwd(const uint16_t* src, uint16_t* dst, const float* w, const float* cs,
+                     const float* sn, int hd, float eps, int rotate, int mode, float* buf) {
+  const int half = hd / 2;
+  for (int i = 0; i < hd; ++i) {
+    const float v = orc_bf16_to_f32(src[i]);
+    buf[i] = v * v;
+  }
+  const float ss = (mode == ROUND_INTERP)
+                       ? orc_numpy_sum(buf, half) + orc_numpy_sum(buf + half, half)
+                       : orc_canonical_sum(buf, hd, hd / 8);
+  const float rstd = 1.0f / sqrtf(ss / (float)hd + eps);
+  for (int i = 0; i < hd; ++i) buf[i] = rbf((orc_bf16_to_f32(src[i]) * rstd) * w[i], mode);
+  for (int i = 0; i < hd; ++i) {
+    float o = buf[i];
+    if (rotate) {
+      const int j = i % half;
+      o = (i < half) ? (buf[i] * cs[j]) - (buf[i + half] * sn[j])
+                     : (buf[i] * cs[j]) + (buf[i - half] * sn[j]);
+    }
+    dst[i] = orc_f32_to_bf16(o, mode);
+  }
+}
+
+/* src/kernels/rope.py:61-143.  qkv [B,S,3,H,hd]; q, k (and v if non-null)
+ * [B,S,H,hd]; cos, sin [S, hd/2]; position = token % S. */
+void orc_qkv_norm_rope(const uint16_t* qkv, const float* qw, const float* kw, const float* cs,
+                       const float* sn, uint16_t* q, uint16_t* k, uint16_t* v, int64_t B,
+                       int64_t S, int64_t H, int64_t hd, float eps, int mode) {
+  float* buf = (float*)malloc((size_t)hd * sizeof(float));
+  const int64_t width = H * hd;
+  for (int64_t tok = 0; tok < B * S; ++tok) {
+    const int64_t pos = tok % S;
+    const uint16_t* row = qkv + tok * 3 * width;
+    for (int64_t h = 0; h < H; ++h) {
+      head_fwd(row + h * hd, q + tok * width + h * hd, qw, cs + pos * hd / 2, sn + pos * hd / 2,
+               (int)hd, eps, 1, mode, buf);
+      head_fwd(row + width + h * hd, k + tok * width + h * hd, kw, cs + pos * hd / 2,
+               sn + pos * hd / 2, (int)hd, eps, 1, mode, buf);
+    }
+    if (v) memcpy(v + tok * width, row + 2 * width, (size_t)width * sizeof(uint16_t));
+  }
+  free(buf);
+}
+
+/* src/kernels/rope.py:146-172.  x [B,S,H*hd] -> y [B,S,H,hd]. */
+void orc_head_norm(const uint16_t* x, const float* w, uint16_t* y, int64_t B, int64_t S,
+                   int64_t H, int64_t hd, float eps, int mode) {
+  float* buf = (float*)malloc((size_t)hd * sizeof(float));
+  for (int64_t tok = 0; tok < B * S; ++tok)
+    for (int64_t h = 0; h < H; ++h)
+      head_fwd(x + (tok * H + h) * hd, y + (tok * H + h) * hd, w, NULL, NULL, (int)hd, eps, 0,
+               mode, buf);
+  free(buf);
+}

@@ -1,0 +1,153 @@
+"""Generate golden vectors by running the reference's own Triton kernels.
+
+    python tests/golden/gen_golden.py [--reference PATH]
+
+Imports tan0210/anima-flat's src/kernels (default PATH /root/reference, read
+only) with TRITON_INTERPRET=1, launches each hot-path kernel through its
+JITFunction (``kernel.fn[grid](...)``, bypassing the GPU-only autotuner) on
+small seeded CPU inputs, and writes the inputs and outputs to
+tests/golden/<case>.npz.  bf16 tensors are stored as uint16 bit patterns,
+e4m3 as uint8.  The interpreter truncates fp32->bf16 casts and evaluates
+tl.sum with numpy; the oracle's INTERP mode reproduces both, and the tests
+compare it with these files.  Only this script reads the reference; the
+fixtures are what the tests use.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+OUT = Path(__file__).resolve().parent
+
+
+def bits(t):
+    import torch
+
+    if t.dtype == torch.bfloat16:
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+    if t.dtype == torch.float8_e4m3fn:
+        return t.contiguous().view(torch.uint8).numpy().copy()
+    return t.contiguous().numpy().copy()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    os.environ["TRITON_INTERPRET"] = "1"
+    sys.path.insert(0, args.reference)
+    import torch
+    import triton
+    from src.kernels import adaln as A
+    from src.kernels import fp8 as F8
+    from src.kernels import rope as R
+    from src.model import rope_tables
+
+    bf = torch.bfloat16
+    gen = torch.Generator().manual_seed(20261201)
+
+    def randn(*shape, std=1.0, outliers=0.0):
+        t = torch.randn(*shape, generator=gen) * std
+        if outliers:
+            m = torch.rand(*shape, generator=gen) < outliers
+            t = torch.where(m, t * 20.0, t)
+        return t
+
+    def mods(B, D):
+        shift = randn(B, D, std=0.1).to(bf)
+        scale = (1.0 + randn(B, D, std=0.1)).to(bf)
+        gate = randn(B, D, std=0.1).to(bf)
+        return shift, scale, gate
+
+    def save(name, **arrays):
+        np.savez_compressed(OUT / f"{name}.npz", **{k: bits(v) if isinstance(v, torch.Tensor) else v
+                                                     for k, v in arrays.items()})
+        print("wrote", name, {k: getattr(v, "shape", v) for k, v in arrays.items()})
+
+    # --- AdaLN / residual AdaLN (adaln.py:10-46) -------------------------------------
+    for name, (B, S, D, has_x, outl) in {
+        "residual_adaln_d2048": (2, 3, 2048, True, 0.0),
+        "adaln_d2048": (2, 3, 2048, False, 0.0),
+        "residual_adaln_d256": (1, 5, 256, True, 0.01),
+    }.items():
+        x = randn(B, S, D, outliers=outl).to(bf)
+        res = randn(B, S, D, outliers=outl).to(bf)
+        shift, scale, gate = mods(B, D)
+        h = torch.empty_like(res)
+        z = torch.empty_like(res)
+        if has_x:
+            A._residual_adaln_kernel.fn[(B * S,)](x, res, gate, shift, scale, h, z, S, 1e-6,
+                                                  D=D, BLOCK=triton.next_power_of_2(D), HAS_X=True)
+            save(name, x=x, res=res, gate=gate, shift=shift, scale=scale, h=h, z=z,
+                 eps=np.float32(1e-6))
+        else:
+            A._residual_adaln_kernel.fn[(B * S,)](res, res, shift, shift, scale, h, h, S, 1e-6,
+                                                  D=D, BLOCK=triton.next_power_of_2(D), HAS_X=False)
+            save(name, res=res, shift=shift, scale=scale, h=h, eps=np.float32(1e-6))
+
+    # --- FP8 AdaLN (fp8.py:56-97) -----------------------------------------------------
+    for name, has_x in {"residual_adaln_fp8_d2048": True, "adaln_fp8_d2048": False}.items():
+        B, S, D = 2, 3, 2048
+        x = randn(B, S, D, outliers=0.01).to(bf)
+        res = randn(B, S, D, outliers=0.01).to(bf)
+        shift, scale, gate = mods(B, D)
+        q = torch.empty(B, S, D, dtype=torch.float8_e4m3fn)
+        s = torch.empty(B * S, 1, dtype=torch.float32)
+        z = torch.empty_like(res)
+        if has_x:
+            F8._residual_adaln_fp8_kernel.fn[(B * S,)](x, res, gate, shift, scale, q, s, z, S, 1e-6,
+                                                       D=D, BLOCK=D, HAS_X=True)
+            save(name, x=x, res=res, gate=gate, shift=shift, scale=scale, q=q, s=s, z=z,
+                 eps=np.float32(1e-6))
+        else:
+            F8._residual_adaln_fp8_kernel.fn[(B * S,)](res, res, shift, shift, scale, q, s, res, S,
+                                                       1e-6, D=D, BLOCK=D, HAS_X=False)
+            save(name, res=res, shift=shift, scale=scale, q=q, s=s, eps=np.float32(1e-6))
+
+    # --- rowquant (fp8.py:273-292) ----------------------------------------------------
+    for name, (rows, K, gelu) in {
+        "rowquant_k2048": (6, 2048, False),
+        "rowquant_k8192": (4, 8192, False),
+        "rowquant_gelu_k8192": (4, 8192, True),
+        "rowquant_gelu_k2048": (6, 2048, True),
+    }.items():
+        x = randn(1, rows, K, outliers=0.01).to(bf)
+        q = torch.empty(1, rows, K, dtype=torch.float8_e4m3fn)
+        s = torch.empty(rows, 1, dtype=torch.float32)
+        F8._rowquant_kernel.fn[(rows,)](x, q, s, K=K, BLOCK=K, GELU=gelu)
+        save(name, x=x, q=q, s=s, gelu=np.bool_(gelu))
+
+    # --- q/k RMSNorm + RoPE and head norm (rope.py:12-172) ----------------------------
+    for name, (B, hh, ww, H, hd, eps) in {
+        "qkv_norm_rope_h4": (2, 4, 4, 4, 128, 1e-5),
+        "qkv_norm_rope_eps1e6": (1, 2, 3, 2, 128, 1e-6),
+    }.items():
+        S = hh * ww
+        cos, sin = rope_tables(hh, ww, hd, "cpu", (4.0, 4.0))
+        qkv = randn(B, S, 3 * H * hd).to(bf)
+        qw = 1.0 + randn(hd, std=0.02)
+        kw = 1.0 + randn(hd, std=0.02)
+        q = torch.empty(B, S, H, hd, dtype=bf)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+        hpp = 2
+        R._qkv_norm_rope_kernel.fn[(B * S, 3 * triton.cdiv(H, hpp))](
+            qkv, q, k, v, qw, kw, cos, sin, S, eps, HEADS=H, HALF=hd // 2, HPP=hpp)
+        save(name, qkv=qkv, qw=qw, kw=kw, cos=cos, sin=sin, q=q, k=k, v=v, heads=np.int64(H),
+             eps=np.float32(eps))
+
+    B, S, H, hd = 2, 5, 4, 128
+    x = randn(B, S, H * hd).to(bf)
+    w = 1.0 + randn(hd, std=0.02)
+    y = torch.empty(B, S, H, hd, dtype=bf)
+    R._head_norm_kernel.fn[(B * S, triton.cdiv(H, 2))](x, y, w, 1e-5, HEADS=H, HALF=hd // 2, HPP=2)
+    save("head_norm_h4", x=x, w=w, y=y, heads=np.int64(H), eps=np.float32(1e-5))
+
+
+if __name__ == "__main__":
+    main()

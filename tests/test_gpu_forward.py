@@ -1,0 +1,238 @@
+"""Forward kernels on the GPU against the CPU oracle (bit-exact) and the torch
+fp32 formulation (2 bf16 ulp).  Inputs are seeded on the CPU so both sides
+see identical bits; every call goes through the public API and the C ABI."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import anima_flat_b200 as afb
+from anima_flat_b200 import _lib
+from oracle import canonical as C
+from oracle import formulation as Fm
+from tests.conftest import from_bits, to_bits, ulp_diff_ok
+
+pytestmark = pytest.mark.gpu
+
+
+def rng(seed):
+    return np.random.default_rng(seed)
+
+
+def bf_bits(a: np.ndarray) -> np.ndarray:
+    return to_bits(torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16))
+
+
+def act(r, shape, outliers=0.0, std=1.0):
+    a = r.standard_normal(shape, dtype=np.float32) * std
+    if outliers:
+        a = np.where(r.random(shape) < outliers, a * 20.0, a)
+    return bf_bits(a)
+
+
+def mods(r, B, D):
+    return (bf_bits(r.standard_normal((B, D), dtype=np.float32) * 0.1),        # shift
+            bf_bits(1.0 + r.standard_normal((B, D), dtype=np.float32) * 0.1),  # scale (+1)
+            bf_bits(r.standard_normal((B, D), dtype=np.float32) * 0.1))        # gate
+
+
+def dev(a, cuda_dev):
+    return from_bits(a, cuda_dev)
+
+
+ADALN_SHAPES = [(1, 1, 2048), (2, 3, 2048), (1, 4096, 2048), (2, 37, 1024), (3, 5, 256),
+                (1, 7, 4096), (1, 9, 8), (2, 11, 2040), (1, 3, 520)]
+
+
+@pytest.mark.parametrize("B,S,D", ADALN_SHAPES)
+def test_residual_adaln_bit_exact(B, S, D, cuda_dev):
+    r = rng(B * 1000 + S + D)
+    x, res = act(r, (B, S, D)), act(r, (B, S, D))
+    shift, scale, gate = mods(r, B, D)
+    h, z = afb.residual_adaln(*(dev(a, cuda_dev) for a in (x, res, gate, shift, scale)))
+    o = C.adaln_fwd(res, shift, scale, x=x, gate=gate)
+    np.testing.assert_array_equal(to_bits(z), o["z"])
+    np.testing.assert_array_equal(to_bits(h), o["h"])
+
+
+@pytest.mark.parametrize("B,S,D", ADALN_SHAPES)
+def test_adaln_bit_exact(B, S, D, cuda_dev):
+    r = rng(B * 2000 + S + D)
+    z = act(r, (B, S, D), outliers=0.01)
+    shift, scale, _ = mods(r, B, D)
+    h = afb.adaln(*(dev(a, cuda_dev) for a in (z, shift, scale)))
+    o = C.adaln_fwd(z, shift, scale)
+    np.testing.assert_array_equal(to_bits(h), o["h"])
+
+
+@pytest.mark.parametrize("B,S,D", [(1, 1, 2048), (2, 4096, 2048), (2, 37, 1024), (3, 5, 256),
+                                   (1, 7, 4096), (2, 11, 2040)])
+@pytest.mark.parametrize("has_x", [True, False])
+def test_adaln_fp8_bit_exact(B, S, D, has_x, cuda_dev):
+    r = rng(B * 3000 + S + D + has_x)
+    x, res = act(r, (B, S, D), 0.01), act(r, (B, S, D), 0.01)
+    shift, scale, gate = mods(r, B, D)
+    if has_x:
+        q, s, z = afb.residual_adaln_fp8(*(dev(a, cuda_dev) for a in (x, res, gate, shift, scale)))
+        o = C.adaln_fwd(res, shift, scale, x=x, gate=gate, fp8=True)
+        np.testing.assert_array_equal(to_bits(z), o["z"])
+    else:
+        q, s = afb.adaln_fp8(*(dev(a, cuda_dev) for a in (res, shift, scale)))
+        o = C.adaln_fwd(res, shift, scale, fp8=True)
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (B * S, 1) and s.dtype == torch.float32
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), o["s"].view(np.uint32))
+    np.testing.assert_array_equal(to_bits(q), o["q"])
+
+
+@pytest.mark.parametrize("rows,K", [(1, 16), (7, 2048), (8192, 2048), (5, 2064), (3, 4096),
+                                    (9, 8192), (2, 16384), (4, 6144)])
+def test_rowquant_bit_exact(rows, K, cuda_dev):
+    r = rng(rows + K)
+    x = act(r, (1, rows, K), 0.01)
+    q, s = afb.rowquant(dev(x, cuda_dev), gelu=False)
+    oq, os_ = C.rowquant(x)
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), os_.view(np.uint32))
+    np.testing.assert_array_equal(to_bits(q), oq)
+
+
+def _codes_at_ties_only(q_bits, y, s):
+    """Codes equal e4m3(y/s) except where y/s is within 4 fp32 ulp of an e4m3 tie."""
+    rows = s.shape[0]
+    v = np.clip((y.reshape(rows, -1) / s.reshape(rows, 1)).astype(np.float32), -448, 448)
+    exact = torch.from_numpy(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    bad = q_bits.reshape(rows, -1) != exact
+    if bad.any():
+        lo, hi = v[bad], v[bad]
+        for _ in range(4):
+            lo = np.nextafter(lo, -np.inf, dtype=np.float32)
+            hi = np.nextafter(hi, np.inf, dtype=np.float32)
+        c = lambda a: torch.from_numpy(a).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+        assert np.all(c(lo) != c(hi)), "an FP8 code differs away from a rounding tie"
+    return int(bad.sum())
+
+
+@pytest.mark.parametrize("rows,K,outliers", [(7, 2048, 0.01), (8192, 8192, 0.01), (256, 8192, 0.0),
+                                             (64, 2048, 0.0), (3, 16384, 0.0), (5, 16, 0.0)])
+def test_rowquant_gelu_scale_exact_codes_at_ties(rows, K, outliers, cuda_dev):
+    r = rng(rows * 7 + K)
+    x = act(r, (1, rows, K), outliers)
+    q, s = afb.rowquant(dev(x, cuda_dev), gelu=True)
+    oq, os_, oy = C.rowquant(x, gelu=True, want_y=True)
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), os_.view(np.uint32))
+    _codes_at_ties_only(to_bits(q), oy, os_)
+
+
+def test_gelu_probe_exhaustive(cuda_dev):
+    """Over all finite bf16 inputs: the device canonical GELU equals the
+    oracle's bit for bit, and the fast GELU stays within the bound the row
+    kernel relies on (|fast - canon| <= 2^-20 + 2^-12 |canon|)."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    vals = (bits.astype(np.uint32) << 16).view(np.float32)
+    bits = bits[np.isfinite(vals)]
+    x = torch.from_numpy(bits.view(np.int16)).to(cuda_dev)
+    fast = torch.empty(x.numel(), dtype=torch.float32, device=cuda_dev)
+    canon = torch.empty_like(fast)
+    _lib.call("afb_gelu_probe", x.data_ptr(), fast.data_ptr(), canon.data_ptr(), x.numel(),
+              torch.cuda.current_stream().cuda_stream)
+    canon_h = canon.cpu().numpy()
+    np.testing.assert_array_equal(canon_h.view(np.uint32), C.gelu(bits).view(np.uint32))
+    f = fast.cpu().numpy().astype(np.float64)
+    c = canon_h.astype(np.float64)
+    bound = 2.0 ** -20 + 2.0 ** -12 * np.abs(c)
+    assert np.all(np.abs(f - c) <= bound)
+
+
+QKV_CASES = [(1, 4096, 16, 128, 1e-5), (2, 16, 4, 128, 1e-5), (1, 6, 3, 64, 1e-6),
+             (1, 5, 2, 256, 1e-5), (2, 7, 5, 128, 1e-6), (3, 1, 16, 128, 1e-5)]
+
+
+def qkv_inputs(r, B, S, H, hd):
+    qkv = act(r, (B, S, 3 * H * hd))
+    qw = (1.0 + r.standard_normal(hd) * 0.02).astype(np.float32)
+    kw = (1.0 + r.standard_normal(hd) * 0.02).astype(np.float32)
+    ang = r.random((S, hd // 2)).astype(np.float32) * 6.0
+    return qkv, qw, kw, np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+@pytest.mark.parametrize("B,S,H,hd,eps", QKV_CASES)
+def test_qkv_norm_rope_bit_exact(B, S, H, hd, eps, cuda_dev):
+    r = rng(B + S + H + hd)
+    qkv, qw, kw, cos, sin = qkv_inputs(r, B, S, H, hd)
+    args = [from_bits(a, cuda_dev) for a in (qkv, qw, kw, cos, sin)]
+    with torch.no_grad():
+        q, k, v = afb.qkv_norm_rope(*args, H, eps)
+    oq, ok, _ = C.qkv_norm_rope(qkv, qw, kw, cos, sin, H, eps)
+    np.testing.assert_array_equal(to_bits(q), oq)
+    np.testing.assert_array_equal(to_bits(k), ok)
+    assert v.data_ptr() == args[0].data_ptr() + 2 * H * hd * 2  # strided view of qkv
+    # grad mode copies v through the kernel
+    qkv_g = args[0].clone().requires_grad_(True)
+    q2, k2, v2 = afb.qkv_norm_rope(qkv_g, *args[1:], H, eps)
+    np.testing.assert_array_equal(to_bits(q2), oq)
+    np.testing.assert_array_equal(to_bits(v2), qkv.reshape(B, S, 3, H, hd)[:, :, 2])
+
+
+@pytest.mark.parametrize("B,S,H,hd", [(1, 4096, 16, 128), (2, 5, 4, 128), (1, 3, 7, 64), (2, 2, 3, 256)])
+def test_head_norm_bit_exact(B, S, H, hd, cuda_dev):
+    r = rng(B * 11 + S + H + hd)
+    x = act(r, (B, S, H * hd))
+    w = (1.0 + r.standard_normal(hd) * 0.02).astype(np.float32)
+    y = afb.head_norm(from_bits(x, cuda_dev), from_bits(w, cuda_dev), H, 1e-5)
+    np.testing.assert_array_equal(to_bits(y), C.head_norm(x, w, H, 1e-5))
+
+
+def test_config2_within_2_ulp_of_torch_fp32(cuda_dev):
+    """The config-2 shapes against the reference's unfused torch fp32 composition."""
+    r = rng(2)
+    B, S, D, H, hd = 1, 4096, 2048, 16, 128
+    x, res = act(r, (B, S, D)), act(r, (B, S, D))
+    shift, scale, gate = mods(r, B, D)
+    t = [dev(a, cuda_dev) for a in (x, res, gate, shift, scale)]
+    h, z = afb.residual_adaln(*t)
+    h_ref, z_ref = Fm.residual_adaln(*t)
+    assert torch.equal(z, z_ref)
+    ok, worst = ulp_diff_ok(to_bits(h), Fm.adaln_y(z_ref, t[3], t[4], 1e-6).cpu().numpy())
+    assert ok, worst
+    qkv, qw, kw, cos, sin = qkv_inputs(r, B, S, H, hd)
+    a = [from_bits(v, cuda_dev) for v in (qkv, qw, kw, cos, sin)]
+    with torch.no_grad():
+        q, k, _ = afb.qkv_norm_rope(*a, H, 1e-5)
+    qr, kr, _ = Fm.qkv_norm_rope(*a, H, 1e-5)
+    # rotation inputs are the bf16-rounded normed values; compare against fp32 rotation
+    assert (q.float() - qr.float()).abs().max() <= 2 * 2.0 ** -7 * qr.float().abs().max()
+    assert (k.float() - kr.float()).abs().max() <= 2 * 2.0 ** -7 * kr.float().abs().max()
+
+
+def test_pdl_off_gives_identical_results(cuda_dev):
+    r = rng(5)
+    B, S, D = 2, 300, 2048
+    x, res = act(r, (B, S, D)), act(r, (B, S, D))
+    shift, scale, gate = mods(r, B, D)
+    t = [dev(a, cuda_dev) for a in (x, res, gate, shift, scale)]
+    h1, z1 = afb.residual_adaln(*t)
+    _lib.set_pdl(False)
+    try:
+        h2, z2 = afb.residual_adaln(*t)
+    finally:
+        _lib.set_pdl(True)
+    assert torch.equal(h1, h2) and torch.equal(z1, z2)
+
+
+def test_side_stream_and_noncontiguous_modulation(cuda_dev):
+    """Launches follow the current stream; strided [B, D] views are accepted
+    (the final layer passes fin.chunk(2, -1) halves, model.py:374-375)."""
+    r = rng(6)
+    B, S, D = 2, 64, 2048
+    x, res = act(r, (B, S, D)), act(r, (B, S, D))
+    shift, scale, gate = mods(r, B, D)
+    t = [dev(a, cuda_dev) for a in (x, res, gate, shift, scale)]
+    fin = torch.cat([t[3], t[4]], dim=-1)
+    sh_view, sc_view = fin.chunk(2, dim=-1)
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        h, z = afb.residual_adaln(t[0], t[1], t[2], sh_view, sc_view)
+    side.synchronize()
+    o = C.adaln_fwd(res, shift, scale, x=x, gate=gate)
+    np.testing.assert_array_equal(to_bits(h), o["h"])

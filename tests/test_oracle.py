@@ -1,0 +1,228 @@
+"""The CPU oracle against the reference (CPU only).
+
+1. Pin: in INTERP mode the oracle must reproduce, bit for bit, the outputs
+   of the reference's own Triton kernels run under TRITON_INTERPRET=1
+   (tests/golden/*.npz, made by tests/golden/gen_golden.py).
+2. Formulation: in RNE mode (the mode the CUDA kernels are held to) bf16
+   outputs stay within 2 bf16 ulp of the reference's unfused torch fp32
+   composition, FP8 scales within 1 fp32 ulp, FP8 codes equal except at
+   rounding ties.
+3. Casts: the oracle's bf16 and e4m3 roundings equal torch's.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import canonical as C
+from oracle import formulation as Fm
+from tests.conftest import from_bits, golden, to_bits, ulp_diff_ok
+
+ADALN_CASES = ["residual_adaln_d2048", "adaln_d2048", "residual_adaln_d256"]
+FP8_CASES = ["residual_adaln_fp8_d2048", "adaln_fp8_d2048"]
+ROWQUANT_CASES = ["rowquant_k2048", "rowquant_k8192", "rowquant_gelu_k2048", "rowquant_gelu_k8192"]
+ROPE_CASES = ["qkv_norm_rope_h4", "qkv_norm_rope_eps1e6"]
+
+
+# ----------------------------------------------------------------------- pin --
+@pytest.mark.parametrize("name", ADALN_CASES)
+def test_pin_adaln(name):
+    g = golden(name)
+    o = C.adaln_fwd(g["res"], g["shift"], g["scale"], x=g.get("x"), gate=g.get("gate"),
+                    eps=float(g["eps"]), mode=C.INTERP)
+    np.testing.assert_array_equal(o["h"], g["h"])
+    if "x" in g:
+        np.testing.assert_array_equal(o["z"], g["z"])
+
+
+@pytest.mark.parametrize("name", FP8_CASES)
+def test_pin_adaln_fp8(name):
+    g = golden(name)
+    o = C.adaln_fwd(g["res"], g["shift"], g["scale"], x=g.get("x"), gate=g.get("gate"),
+                    eps=float(g["eps"]), fp8=True, mode=C.INTERP)
+    np.testing.assert_array_equal(o["q"], g["q"])
+    np.testing.assert_array_equal(o["s"], g["s"])
+    if "x" in g:
+        np.testing.assert_array_equal(o["z"], g["z"])
+
+
+@pytest.mark.parametrize("name", ROWQUANT_CASES)
+def test_pin_rowquant(name):
+    g = golden(name)
+    q, s = C.rowquant(g["x"], gelu=bool(g["gelu"]), mode=C.INTERP)
+    np.testing.assert_array_equal(q, g["q"])
+    np.testing.assert_array_equal(s, g["s"])
+
+
+@pytest.mark.parametrize("name", ROPE_CASES)
+def test_pin_qkv_norm_rope(name):
+    g = golden(name)
+    q, k, v = C.qkv_norm_rope(g["qkv"], g["qw"], g["kw"], g["cos"], g["sin"], int(g["heads"]),
+                              eps=float(g["eps"]), with_v=True, mode=C.INTERP)
+    np.testing.assert_array_equal(q, g["q"])
+    np.testing.assert_array_equal(k, g["k"])
+    np.testing.assert_array_equal(v, g["v"])
+
+
+def test_pin_head_norm():
+    g = golden("head_norm_h4")
+    y = C.head_norm(g["x"], g["w"], int(g["heads"]), eps=float(g["eps"]), mode=C.INTERP)
+    np.testing.assert_array_equal(y, g["y"])
+
+
+def test_pin_tables():
+    """The rope tables restated in the package equal the fixture's (model.py:51-84)."""
+    from anima_flat_b200.tables import rope_tables
+
+    g = golden("qkv_norm_rope_h4")
+    cos, sin = rope_tables(4, 4, 128, "cpu", (4.0, 4.0))
+    np.testing.assert_array_equal(cos.numpy(), g["cos"])
+    np.testing.assert_array_equal(sin.numpy(), g["sin"])
+
+
+# -------------------------------------------------------------- formulation --
+def _t(a):
+    return from_bits(a)
+
+
+@pytest.mark.parametrize("name", ADALN_CASES)
+def test_formulation_adaln(name):
+    g = golden(name)
+    o = C.adaln_fwd(g["res"], g["shift"], g["scale"], x=g.get("x"), gate=g.get("gate"),
+                    eps=float(g["eps"]))
+    if "x" in g:
+        z = Fm.residual_z(_t(g["x"]), _t(g["res"]), _t(g["gate"]))
+        np.testing.assert_array_equal(o["z"], to_bits(z))
+        y = Fm.adaln_y(z, _t(g["shift"]), _t(g["scale"]), float(g["eps"]))
+    else:
+        y = Fm.adaln_y(_t(g["res"]), _t(g["shift"]), _t(g["scale"]), float(g["eps"]))
+    ok, worst = ulp_diff_ok(o["h"], y.numpy(), 2.0)
+    assert ok, f"worst {worst} bf16 ulp"
+
+
+@pytest.mark.parametrize("name", FP8_CASES)
+def test_formulation_adaln_fp8(name):
+    g = golden(name)
+    o = C.adaln_fwd(g["res"], g["shift"], g["scale"], x=g.get("x"), gate=g.get("gate"),
+                    eps=float(g["eps"]), fp8=True)
+    z = Fm.residual_z(_t(g["x"]), _t(g["res"]), _t(g["gate"])) if "x" in g else _t(g["res"])
+    y = Fm.adaln_y(z, _t(g["shift"]), _t(g["scale"]), float(g["eps"]))
+    q_ref, s_ref = Fm.quantize_rows(y)
+    s_ref = s_ref.numpy()
+    assert np.all(np.abs(o["s"].view(np.int32) - s_ref.view(np.int32)) <= 1)
+    _codes_differ_only_at_ties(o["q"], y.numpy(), o["s"])
+
+
+@pytest.mark.parametrize("name", ROWQUANT_CASES)
+def test_formulation_rowquant(name):
+    g = golden(name)
+    gelu = bool(g["gelu"])
+    q, s, y = C.rowquant(g["x"], gelu=gelu, want_y=True)
+    y_ref = Fm.gelu_as(_t(g["x"])) if gelu else _t(g["x"]).float()
+    assert np.abs(y.astype(np.float64) - y_ref.numpy()).max() <= 2e-6 * max(1.0, np.abs(y).max())
+    _, s_ref = Fm.quantize_rows(y_ref)
+    if not gelu:
+        np.testing.assert_array_equal(s, s_ref.numpy())
+    else:
+        assert np.all(np.abs(s.view(np.int32) - s_ref.numpy().view(np.int32)) <= 2)
+    _codes_differ_only_at_ties(q, y, s)
+
+
+def _codes_differ_only_at_ties(q: np.ndarray, y: np.ndarray, s: np.ndarray) -> None:
+    """Codes must equal e4m3(y / s) except where y / s is within 4 fp32 ulp of a tie."""
+    rows = s.shape[0]
+    v = (y.reshape(rows, -1).astype(np.float32) / s.reshape(rows, 1)).astype(np.float32)
+    v = np.clip(v, -448.0, 448.0)
+    exact = torch.from_numpy(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    qq = q.reshape(rows, -1)
+    bad = qq != exact
+    if not bad.any():
+        return
+    lo = np.nextafter(v, -np.inf, dtype=np.float32)
+    hi = np.nextafter(v, np.inf, dtype=np.float32)
+    for _ in range(3):
+        lo = np.nextafter(lo, -np.inf, dtype=np.float32)
+        hi = np.nextafter(hi, np.inf, dtype=np.float32)
+    c_lo = torch.from_numpy(lo).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    c_hi = torch.from_numpy(hi).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    near_tie = c_lo != c_hi
+    assert np.all(near_tie[bad]), f"{int((bad & ~near_tie).sum())} codes differ away from a tie"
+
+
+@pytest.mark.parametrize("name", ROPE_CASES)
+def test_formulation_qkv_norm_rope(name):
+    g = golden(name)
+    H, eps = int(g["heads"]), float(g["eps"])
+    q, k, v = C.qkv_norm_rope(g["qkv"], g["qw"], g["kw"], g["cos"], g["sin"], H, eps=eps,
+                              with_v=True)
+    qkv = _t(g["qkv"])
+    B, S, W = qkv.shape
+    hd = W // (3 * H)
+    qr, kr, _ = qkv.view(B, S, 3, H, hd).unbind(2)
+    cos, sin = torch.from_numpy(g["cos"]), torch.from_numpy(g["sin"])
+    for ours, part, w in ((q, qr, g["qw"]), (k, kr, g["kw"])):
+        n = Fm._rms_heads(part, torch.from_numpy(w), eps)
+        half = hd // 2
+        a, b = n.float()[..., :half], n.float()[..., half:]
+        c, s = cos[None, :, None, :], sin[None, :, None, :]
+        y = torch.cat([a * c - b * s, b * c + a * s], dim=-1)
+        ok, worst = ulp_diff_ok(ours, y.numpy(), 2.0)
+        assert ok, f"worst {worst} bf16 ulp"
+    np.testing.assert_array_equal(v, g["qkv"].reshape(B, S, 3, H, hd)[:, :, 2])
+
+
+def test_formulation_head_norm():
+    g = golden("head_norm_h4")
+    H, eps = int(g["heads"]), float(g["eps"])
+    y = C.head_norm(g["x"], g["w"], H, eps=eps)
+    x = _t(g["x"])
+    B, S, W = x.shape
+    xf = x.float().view(B, S, H, W // H)
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * torch.from_numpy(g["w"])
+    ok, worst = ulp_diff_ok(y, ref.numpy(), 2.0)
+    assert ok, f"worst {worst} bf16 ulp"
+
+
+# -------------------------------------------------------------------- casts --
+def test_e4m3_cast_matches_torch():
+    rng = np.random.default_rng(3)
+    v = np.concatenate([
+        rng.standard_normal(20000) * rng.choice([1e-4, 1e-2, 1.0, 10.0, 100.0], 20000),
+        np.arange(-448.0, 448.01, 0.0625),
+        np.arange(-0.03, 0.03, 2.0 ** -13),
+    ]).astype(np.float32)
+    v = np.clip(v, -448.0, 448.0)
+    ours = np.array([C.lib().orc_f32_to_e4m3(float(x), C.RNE) for x in v], dtype=np.uint8)
+    ref = torch.from_numpy(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(ours, ref)
+
+
+def test_bf16_rounding_matches_torch():
+    rng = np.random.default_rng(4)
+    x = torch.from_numpy((rng.standard_normal(4096) * rng.choice([1e-20, 1e-3, 1.0, 1e3], 4096))
+                         .astype(np.float32))
+    res = C.adaln_fwd(np.zeros((1, 1, 8), np.uint16), np.zeros((1, 8), np.uint16),
+                      np.zeros((1, 8), np.uint16))  # exercise the library
+    assert res["h"].shape == (1, 1, 8)
+    bits = to_bits(x.to(torch.bfloat16))
+    import ctypes
+
+    f = C.lib().orc_f32_to_bf16
+    f.argtypes = [ctypes.c_float, ctypes.c_int]
+    f.restype = ctypes.c_uint16
+    ours = np.array([f(float(t), C.RNE) for t in x.numpy()], dtype=np.uint16)
+    np.testing.assert_array_equal(ours, bits)
+
+
+def test_canonical_sum_definition():
+    """The canonical order on a small case, spelled out by hand."""
+    x = np.arange(1, 513, dtype=np.float32) * np.float32(0.1)
+    # 64 vectors -> stride tree to 32 -> intra-vector tree -> stride tree over 32.
+    X = x.reshape(64, 8)
+    X = X[:32] + X[32:]
+    p = ((X[:, 0] + X[:, 1]) + (X[:, 2] + X[:, 3])) + ((X[:, 4] + X[:, 5]) + (X[:, 6] + X[:, 7]))
+    while p.size > 1:
+        p = p[: p.size // 2] + p[p.size // 2:]
+    assert C.canonical_sum(x, 32) == np.float32(p[0])
