@@ -30,6 +30,20 @@ SIGNATURES: dict[str, tuple] = {
     "afb_gelu_probe": (_P, _P, _P, _I, _P),
     "afb_qkv_norm_rope": (_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P),
     "afb_head_norm": (_P, _P, _P, _I, _I, _I, _I, _F, _P),
+    "afb_residual_adaln_bwd": (_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _P,
+                               ctypes.c_size_t, _P),
+    "afb_adaln_bwd": (_P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _P, ctypes.c_size_t, _P),
+    "afb_qkv_norm_rope_bwd": (_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P,
+                              ctypes.c_size_t, _P),
+    "afb_head_norm_bwd": (_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, ctypes.c_size_t, _P),
+}
+
+# Workspace-size queries: name -> argument types (return size_t).
+WORKSPACE_QUERIES: dict[str, tuple] = {
+    "afb_residual_adaln_bwd_workspace": (_I, _I, _I),
+    "afb_adaln_bwd_workspace": (_I, _I, _I),
+    "afb_qkv_norm_rope_bwd_workspace": (_I, _I, _I, _I),
+    "afb_head_norm_bwd_workspace": (_I, _I, _I, _I),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -57,6 +71,10 @@ def load() -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = list(argtypes)
         fn.restype = c_int
+    for name, argtypes in WORKSPACE_QUERIES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = list(argtypes)
+        fn.restype = ctypes.c_size_t
     lib.afb_abi_version.restype = c_int
     lib.afb_abi_version.argtypes = []
     lib.afb_last_error.restype = ctypes.c_char_p
@@ -76,6 +94,16 @@ def call(name: str, *args) -> None:
     if rc != 0:
         msg = lib.afb_last_error().decode(errors="replace")
         raise RuntimeError(f"{name} failed with status {rc}: {msg}")
+
+
+def workspace(name: str, device, *dims: int):
+    """A float32 device buffer of the size the entry point `name` asks for
+    (allocated through torch's caching allocator) and its size in bytes."""
+    import torch
+
+    nbytes = int(getattr(load(), f"{name}_workspace")(*dims))
+    buf = torch.empty(max(1, (nbytes + 3) // 4), dtype=torch.float32, device=device)
+    return buf, nbytes
 
 
 def set_pdl(enabled: bool) -> None:

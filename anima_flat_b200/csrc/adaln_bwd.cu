@@ -1,0 +1,320 @@
+// AdaLN modulate backward (LoRA training), with and without the gated
+// residual.
+//
+// Reference: src/kernels/adaln.py:111-172 (_residual_adaln_bwd_kernel) and
+// :175-217 (_residual_adaln_bwd; partials reduced with torch .sum(1), cast to
+// the parameter dtype).  Per row, with b = row / S and z the saved residual
+// stream:
+//   mean, rstd of z (canonical order, as the forward);  xhat = d * rstd
+//   dxh = gh * scale[b];  c1 = sum(dxh) / D;  c2 = sum(dxh * xhat) / D
+//   dz = rstd * ((dxh - c1) - xhat * c2)  (+ gz)        -> bf16 (dres)
+//   dx = bf16(dz * gate[b])                               (HAS_X)
+//   dshift[b] += gh;  dscale[b] += gh * xhat;  dgate[b] += dz * x   (fp32)
+//
+// Parameter-gradient order (deterministic, independent of the launch shape):
+// the rows of each batch entry are cut into chunks of kChunkRows; in a chunk,
+// warp w sums rows w, w + 4, w + 8, ... in increasing order; the four warp
+// sums combine as a stride tree, (p0 + p2) + (p1 + p3); the finalize kernel adds the chunk
+// sums in increasing chunk order and rounds to bf16.  The chunk sums live in
+// a caller-provided fp32 workspace [B][chunks][NQ][D].
+#include "afb_device.cuh"
+#include "afb_launch.h"
+
+namespace afb {
+
+constexpr int kBwdWarps = 4;
+constexpr int kRowsPerWarp = 4;
+constexpr int kChunkRows = kBwdWarps * kRowsPerWarp;
+
+struct AdalnBwdArgs {
+  const uint16_t* gh;     // [rows, D]
+  const uint16_t* gz;     // [rows, D] or null
+  const uint16_t* z;      // [rows, D]
+  const uint16_t* x;      // [rows, D] (HAS_X)
+  const uint16_t* gate;   // [B, D] (HAS_X)
+  const uint16_t* scale;  // [B, D]
+  uint16_t* dz;           // [rows, D]
+  uint16_t* dx;           // [rows, D] (HAS_X)
+  float* part;            // [B][chunks][NQ][D]
+  int64_t seq;
+  int64_t chunks;         // per batch entry
+  int dim;
+  float eps;
+};
+
+// Shared-memory words per warp: NQ accumulators per column.
+template <bool HAS_X>
+__host__ __device__ constexpr int bwd_nq() { return HAS_X ? 3 : 2; }
+
+template <int NC, bool HAS_X, bool HAS_GZ>
+__global__ void __launch_bounds__(kBwdWarps * 32)
+adaln_bwd_kernel(const AdalnBwdArgs a) {
+  constexpr int NQ = bwd_nq<HAS_X>();
+  extern __shared__ float4 smem4[];
+  float* acc_all = reinterpret_cast<float*>(smem4);
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int D = a.dim;
+  const int64_t b = blockIdx.y;
+  const int64_t chunk = blockIdx.x;
+  const int64_t pbase = b * D;
+  float* acc = acc_all + static_cast<int64_t>(warp) * NQ * D;
+  const float fd = static_cast<float>(D);
+
+  // zero this warp's accumulators (lane owns its own columns)
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int e = (lane + 32 * c) * 8;
+    if (e < D) {
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        reinterpret_cast<float4*>(acc + q * D + e)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        reinterpret_cast<float4*>(acc + q * D + e)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int64_t s = chunk * kChunkRows + i * kBwdWarps + warp;
+    if (s >= a.seq) break;  // warp-uniform
+    const int64_t base = (b * a.seq + s) * D;
+    uint4 zv[NC], gv[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int e = (lane + 32 * c) * 8;
+      const bool ok = e < D;
+      zv[c] = ok ? ld_stream(a.z + base + e) : make_uint4(0, 0, 0, 0);
+      gv[c] = ok ? ld_stream(a.gh + base + e) : make_uint4(0, 0, 0, 0);
+    }
+    // statistics of z, exactly as the forward
+    const float mean = __fdiv_rn(
+        warp_canonical_sum_fn<NC>([&](int c, int k) { return unpack_at(zv[c], k); }), fd);
+    const float rstd = canonical_rstd(
+        __fdiv_rn(warp_canonical_sum_fn<NC>([&](int c, int k) {
+                    const float d = ((lane + 32 * c) * 8 < D) ? __fsub_rn(unpack_at(zv[c], k), mean)
+                                                              : 0.0f;
+                    return __fmul_rn(d, d);
+                  }),
+                  fd),
+        a.eps);
+    // c1 = sum(dxh) / D, c2 = sum(dxh * xhat) / D
+    uint4 scv[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int e = (lane + 32 * c) * 8;
+      scv[c] = (e < D) ? ld_keep(a.scale + pbase + e) : make_uint4(0, 0, 0, 0);
+    }
+    const float c1 = __fdiv_rn(warp_canonical_sum_fn<NC>([&](int c, int k) {
+                                 return __fmul_rn(unpack_at(gv[c], k), unpack_at(scv[c], k));
+                               }),
+                               fd);
+    const float c2 = __fdiv_rn(warp_canonical_sum_fn<NC>([&](int c, int k) {
+                                 if ((lane + 32 * c) * 8 >= D) return 0.0f;
+                                 const float xhat =
+                                     __fmul_rn(__fsub_rn(unpack_at(zv[c], k), mean), rstd);
+                                 const float dxh = __fmul_rn(unpack_at(gv[c], k), unpack_at(scv[c], k));
+                                 return __fmul_rn(dxh, xhat);
+                               }),
+                               fd);
+    // dz, dx and the column accumulators
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int e = (lane + 32 * c) * 8;
+      if (e >= D) continue;
+      float sc[8], g8[8], gz8[8], x8[8], dzf[8];
+      unpack8(scv[c], sc);
+      if (HAS_GZ) unpack8(ld_stream(a.gz + base + e), gz8);
+      if (HAS_X) {
+        unpack8(ld_keep(a.gate + pbase + e), g8);
+        unpack8(ld_stream(a.x + base + e), x8);
+      }
+      float4* a_sh = reinterpret_cast<float4*>(acc + e);
+      float4* a_sc = reinterpret_cast<float4*>(acc + D + e);
+      float sh_acc[8], sc_acc[8], g_acc[8];
+      {
+        const float4 p0 = a_sh[0], p1 = a_sh[1], q0 = a_sc[0], q1 = a_sc[1];
+        sh_acc[0] = p0.x; sh_acc[1] = p0.y; sh_acc[2] = p0.z; sh_acc[3] = p0.w;
+        sh_acc[4] = p1.x; sh_acc[5] = p1.y; sh_acc[6] = p1.z; sh_acc[7] = p1.w;
+        sc_acc[0] = q0.x; sc_acc[1] = q0.y; sc_acc[2] = q0.z; sc_acc[3] = q0.w;
+        sc_acc[4] = q1.x; sc_acc[5] = q1.y; sc_acc[6] = q1.z; sc_acc[7] = q1.w;
+      }
+      if (HAS_X) {
+        const float4* a_g = reinterpret_cast<const float4*>(acc + 2 * D + e);
+        const float4 r0 = a_g[0], r1 = a_g[1];
+        g_acc[0] = r0.x; g_acc[1] = r0.y; g_acc[2] = r0.z; g_acc[3] = r0.w;
+        g_acc[4] = r1.x; g_acc[5] = r1.y; g_acc[6] = r1.z; g_acc[7] = r1.w;
+      }
+      float dxf[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float gh = unpack_at(gv[c], k);
+        const float xhat = __fmul_rn(__fsub_rn(unpack_at(zv[c], k), mean), rstd);
+        const float dxh = __fmul_rn(gh, sc[k]);
+        float dz = __fmul_rn(rstd, __fsub_rn(__fsub_rn(dxh, c1), __fmul_rn(xhat, c2)));
+        if (HAS_GZ) dz = __fadd_rn(dz, gz8[k]);
+        dzf[k] = dz;
+        sh_acc[k] = __fadd_rn(sh_acc[k], gh);
+        sc_acc[k] = __fadd_rn(sc_acc[k], __fmul_rn(gh, xhat));
+        if (HAS_X) {
+          dxf[k] = __fmul_rn(dz, g8[k]);
+          g_acc[k] = __fadd_rn(g_acc[k], __fmul_rn(dz, x8[k]));
+        }
+      }
+      st16(a.dz + base + e, pack8_rn(dzf));
+      if (HAS_X) st16(a.dx + base + e, pack8_rn(dxf));
+      a_sh[0] = make_float4(sh_acc[0], sh_acc[1], sh_acc[2], sh_acc[3]);
+      a_sh[1] = make_float4(sh_acc[4], sh_acc[5], sh_acc[6], sh_acc[7]);
+      a_sc[0] = make_float4(sc_acc[0], sc_acc[1], sc_acc[2], sc_acc[3]);
+      a_sc[1] = make_float4(sc_acc[4], sc_acc[5], sc_acc[6], sc_acc[7]);
+      if (HAS_X) {
+        float4* a_g = reinterpret_cast<float4*>(acc + 2 * D + e);
+        a_g[0] = make_float4(g_acc[0], g_acc[1], g_acc[2], g_acc[3]);
+        a_g[1] = make_float4(g_acc[4], g_acc[5], g_acc[6], g_acc[7]);
+      }
+    }
+  }
+
+  // Chunk partial: stride tree over the warps, (p0 + p2) + (p1 + p3).
+  __syncthreads();
+  float* out = a.part + ((b * a.chunks + chunk) * NQ) * D;
+  const int n = NQ * D;
+  const int64_t stride = static_cast<int64_t>(NQ) * D;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float p0 = acc_all[i], p1 = acc_all[stride + i];
+    const float p2 = acc_all[2 * stride + i], p3 = acc_all[3 * stride + i];
+    out[i] = __fadd_rn(__fadd_rn(p0, p2), __fadd_rn(p1, p3));
+  }
+}
+
+// dparam[b, q, col] = bf16(sum over chunks, in increasing order).
+__global__ void adaln_bwd_finalize_kernel(const float* part, uint16_t* dshift, uint16_t* dscale,
+                                          uint16_t* dgate, int64_t chunks, int nq, int D) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t b = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq * D) return;
+  const float* p = part + b * chunks * nq * D + i;
+  float s = 0.0f;
+  int64_t c = 0;
+  for (; c + 4 <= chunks; c += 4) {
+    const float v0 = p[(c + 0) * nq * D], v1 = p[(c + 1) * nq * D];
+    const float v2 = p[(c + 2) * nq * D], v3 = p[(c + 3) * nq * D];
+    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v0), v1), v2), v3);
+  }
+  for (; c < chunks; ++c) s = __fadd_rn(s, p[c * nq * D]);
+  const int q = i / D, col = i % D;
+  uint16_t* dst = q == 0 ? dshift : q == 1 ? dscale : dgate;
+  dst[b * D + col] = static_cast<uint16_t>(pack2_rn(s, 0.0f) & 0xffffu);
+}
+
+template <bool HAS_X, bool HAS_GZ>
+static cudaError_t launch_adaln_bwd(const AdalnBwdArgs& a, int64_t batch, cudaStream_t st) {
+  constexpr int NQ = bwd_nq<HAS_X>();
+  const size_t smem = static_cast<size_t>(kBwdWarps) * NQ * a.dim * sizeof(float);
+  const dim3 grid(static_cast<unsigned>(a.chunks), static_cast<unsigned>(batch));
+  const dim3 block(kBwdWarps * 32);
+  cudaError_t e = cudaErrorInvalidValue;
+  auto go = [&](auto kern) {
+    cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (r != cudaSuccess) return r;
+    return launch_pdl(kern, grid, block, smem, st, a);
+  };
+  switch (row_chunks(a.dim)) {
+    case 1: e = go(adaln_bwd_kernel<1, HAS_X, HAS_GZ>); break;
+    case 2: e = go(adaln_bwd_kernel<2, HAS_X, HAS_GZ>); break;
+    case 4: e = go(adaln_bwd_kernel<4, HAS_X, HAS_GZ>); break;
+    case 8: e = go(adaln_bwd_kernel<8, HAS_X, HAS_GZ>); break;
+    default: e = cudaErrorInvalidValue; break;
+  }
+  return e;
+}
+
+size_t adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim, bool has_x) {
+  const int64_t chunks = (seq + kChunkRows - 1) / kChunkRows;
+  return static_cast<size_t>(batch * chunks * (has_x ? 3 : 2) * dim) * sizeof(float);
+}
+
+// Shared implementation of the two entry points (and of the workspace-free
+// variant): validates, then launches the row kernel and the finalize kernel.
+int adaln_bwd_impl(const char* name, const void* gh, const void* gz, const void* z,
+                   const void* x, const void* gate, const void* scale, void* dz, void* dx,
+                   void* dgate, void* dshift, void* dscale, int64_t batch, int64_t seq,
+                   int64_t dim, float eps, void* workspace, size_t workspace_bytes,
+                   cudaStream_t st) {
+  ApiGuard g(name);
+  const bool has_x = x != nullptr;
+  if (!check_rows(batch, seq, dim) ||
+      !check(dim <= 2048, "backward supports dim <= 2048, got " + std::to_string(dim)) ||
+      !check_ptrs({gh, z, scale, dz, dshift, dscale}, {"gh", "z", "scale", "dz", "dshift", "dscale"}) ||
+      (gz != nullptr && !check_ptrs({gz}, {"gz"})) ||
+      (has_x && !check_ptrs({gate, dx, dgate}, {"gate", "dx", "dgate"})) ||
+      !check(workspace != nullptr && aligned(workspace, 16), "workspace is null or misaligned") ||
+      !check(workspace_bytes >= adaln_bwd_workspace(batch, seq, dim, has_x),
+             "workspace too small: need " + std::to_string(adaln_bwd_workspace(batch, seq, dim, has_x)) +
+                 " bytes"))
+    return g.fail();
+  if (batch == 0) return 0;
+  AdalnBwdArgs a{};
+  a.gh = static_cast<const uint16_t*>(gh);
+  a.gz = static_cast<const uint16_t*>(gz);
+  a.z = static_cast<const uint16_t*>(z);
+  a.x = static_cast<const uint16_t*>(x);
+  a.gate = static_cast<const uint16_t*>(gate);
+  a.scale = static_cast<const uint16_t*>(scale);
+  a.dz = static_cast<uint16_t*>(dz);
+  a.dx = static_cast<uint16_t*>(dx);
+  a.part = static_cast<float*>(workspace);
+  a.seq = seq;
+  a.chunks = (seq + kChunkRows - 1) / kChunkRows;
+  a.dim = static_cast<int>(dim);
+  a.eps = eps;
+  cudaError_t e;
+  if (has_x) e = gz ? launch_adaln_bwd<true, true>(a, batch, st) : launch_adaln_bwd<true, false>(a, batch, st);
+  else e = gz ? launch_adaln_bwd<false, true>(a, batch, st) : launch_adaln_bwd<false, false>(a, batch, st);
+  if (e != cudaSuccess) return g.done(e);
+  const int nq = has_x ? 3 : 2;
+  const dim3 fgrid(static_cast<unsigned>((nq * dim + 255) / 256), static_cast<unsigned>(batch));
+  e = launch_pdl(adaln_bwd_finalize_kernel, fgrid, dim3(256), 0, st,
+                 static_cast<const float*>(workspace), static_cast<uint16_t*>(dshift),
+                 static_cast<uint16_t*>(dscale), static_cast<uint16_t*>(dgate), a.chunks, nq,
+                 static_cast<int>(dim));
+  return g.done(e);
+}
+
+}  // namespace afb
+
+using namespace afb;
+
+extern "C" size_t afb_residual_adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim) {
+  return adaln_bwd_workspace(batch, seq, dim, true);
+}
+
+extern "C" size_t afb_adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim) {
+  return adaln_bwd_workspace(batch, seq, dim, false);
+}
+
+extern "C" int afb_residual_adaln_bwd(const void* gh, const void* gz, const void* z, const void* x,
+                                      const void* gate, const void* scale, void* dx, void* dres,
+                                      void* dgate, void* dshift, void* dscale, int64_t batch,
+                                      int64_t seq, int64_t dim, float eps, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  if (x == nullptr) {
+    set_error("afb_residual_adaln_bwd: x is null");
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  return adaln_bwd_impl("afb_residual_adaln_bwd", gh, gz, z, x, gate, scale, dres, dx, dgate,
+                        dshift, dscale, batch, seq, dim, eps, workspace, workspace_bytes,
+                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int afb_adaln_bwd(const void* gh, const void* z, const void* scale, void* dz,
+                             void* dshift, void* dscale, int64_t batch, int64_t seq, int64_t dim,
+                             float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  return adaln_bwd_impl("afb_adaln_bwd", gh, nullptr, z, nullptr, nullptr, scale, dz, nullptr,
+                        nullptr, dshift, dscale, batch, seq, dim, eps, workspace, workspace_bytes,
+                        static_cast<cudaStream_t>(stream));
+}

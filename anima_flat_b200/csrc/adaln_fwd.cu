@@ -87,23 +87,16 @@ adaln_fwd_kernel(const AdalnArgs a) {
 
   // Statistics (canonical order, see afb_device.cuh).
   const float fd = static_cast<float>(D);
-  float mean, rstd;
-  {
-    float f[NC][8];
-#pragma unroll
-    for (int c = 0; c < NC; ++c) unpack8(zv[c], f[c]);
-    mean = __fdiv_rn(warp_canonical_sum<NC>(f), fd);
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      const bool ok = (lane + 32 * c) * 8 < D;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float d = ok ? __fsub_rn(unpack_at(zv[c], k), mean) : 0.0f;
-        f[c][k] = __fmul_rn(d, d);
-      }
-    }
-    rstd = canonical_rstd(__fdiv_rn(warp_canonical_sum<NC>(f), fd), a.eps);
-  }
+  const float mean = __fdiv_rn(
+      warp_canonical_sum_fn<NC>([&](int c, int k) { return unpack_at(zv[c], k); }), fd);
+  const float var = __fdiv_rn(warp_canonical_sum_fn<NC>([&](int c, int k) {
+                                const float d = ((lane + 32 * c) * 8 < D)
+                                                    ? __fsub_rn(unpack_at(zv[c], k), mean)
+                                                    : 0.0f;
+                                return __fmul_rn(d, d);
+                              }),
+                              fd);
+  const float rstd = canonical_rstd(var, a.eps);
 
   if (!FP8) {
 #pragma unroll

@@ -148,6 +148,26 @@ __device__ __forceinline__ float warp_canonical_sum(float (&f)[NC][8]) {
   return p;
 }
 
+// The same sum with the elements produced on demand by val(c, k): the first
+// stride level is formed directly from val, so only NC/2 vectors are live.
+template <int NC, typename F>
+__device__ __forceinline__ float warp_canonical_sum_fn(F val) {
+  constexpr int H = NC > 1 ? NC / 2 : 1;
+  float f[H][8];
+#pragma unroll
+  for (int c = 0; c < H; ++c) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if constexpr (NC > 1) {
+        f[c][k] = __fadd_rn(val(c, k), val(c + H, k));
+      } else {
+        f[c][k] = val(c, k);
+      }
+    }
+  }
+  return warp_canonical_sum<H>(f);
+}
+
 // Canonical sum over an aligned group of LPH lanes holding one vector each
 // (P = LPH).  Used for per-head sums (head_dim = 8 * LPH).
 template <int LPH>

@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import torch
 
-from .._lib import call
+from .._lib import call, workspace
 from .common import BF16, _check, _check_dtype, _check_vec, _stream
 
 __all__ = ["adaln", "residual_adaln"]
@@ -60,6 +60,98 @@ def _adaln(z: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, eps: float
 @_adaln.register_fake
 def _(z, shift, scale, eps):
     return torch.empty_like(z)
+
+
+# ------------------------------------------------------------------ backward --
+# adaln.py:175-257.  Per-column gradients of gate/shift/scale are summed over
+# the rows in a fixed order (see csrc/adaln_bwd.cu), so they are reproducible.
+@torch.library.custom_op("anima_flat_b200::residual_adaln_bwd", mutates_args=())
+def _residual_adaln_bwd_op(
+    gh: torch.Tensor,
+    gz: torch.Tensor | None,
+    z: torch.Tensor,
+    x: torch.Tensor,
+    gate: torch.Tensor,
+    scale: torch.Tensor,
+    eps: float,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    B, S, D = z.shape
+    gh = gh.contiguous()
+    gz = gz.contiguous() if gz is not None else None
+    dx = torch.empty_like(x)
+    dres = torch.empty_like(z)
+    dgate = torch.empty_like(gate)
+    dshift = torch.empty_like(scale)
+    dscale = torch.empty_like(scale)
+    ws, nbytes = workspace("afb_residual_adaln_bwd", z.device, B, S, D)
+    call(
+        "afb_residual_adaln_bwd",
+        gh.data_ptr(), gz.data_ptr() if gz is not None else None, z.data_ptr(), x.data_ptr(),
+        gate.data_ptr(), scale.data_ptr(), dx.data_ptr(), dres.data_ptr(), dgate.data_ptr(),
+        dshift.data_ptr(), dscale.data_ptr(), B, S, D, eps, ws.data_ptr(), nbytes, _stream(z),
+    )
+    return dx, dres, dgate, dshift, dscale
+
+
+@_residual_adaln_bwd_op.register_fake
+def _(gh, gz, z, x, gate, scale, eps):
+    return (torch.empty_like(x), torch.empty_like(z), torch.empty_like(gate),
+            torch.empty_like(scale), torch.empty_like(scale))
+
+
+@torch.library.custom_op("anima_flat_b200::adaln_bwd", mutates_args=())
+def _adaln_bwd_op(
+    gh: torch.Tensor, z: torch.Tensor, scale: torch.Tensor, eps: float
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    B, S, D = z.shape
+    gh = gh.contiguous()
+    dz = torch.empty_like(z)
+    dshift = torch.empty_like(scale)
+    dscale = torch.empty_like(scale)
+    ws, nbytes = workspace("afb_adaln_bwd", z.device, B, S, D)
+    call(
+        "afb_adaln_bwd",
+        gh.data_ptr(), z.data_ptr(), scale.data_ptr(), dz.data_ptr(), dshift.data_ptr(),
+        dscale.data_ptr(), B, S, D, eps, ws.data_ptr(), nbytes, _stream(z),
+    )
+    return dz, dshift, dscale
+
+
+@_adaln_bwd_op.register_fake
+def _(gh, z, scale, eps):
+    return torch.empty_like(z), torch.empty_like(scale), torch.empty_like(scale)
+
+
+def _residual_adaln_setup(ctx, inputs, output):
+    x, _, gate, _, scale, eps = inputs
+    ctx.save_for_backward(x, gate, scale, output[1])
+    ctx.eps = eps
+
+
+def _residual_adaln_backward(ctx, gh, gz):
+    x, gate, scale, z = ctx.saved_tensors
+    dx, dres, dgate, dshift, dscale = _residual_adaln_bwd_op(gh, gz, z, x, gate, scale, ctx.eps)
+    return dx, dres, dgate, dshift, dscale, None
+
+
+torch.library.register_autograd(
+    "anima_flat_b200::residual_adaln", _residual_adaln_backward, setup_context=_residual_adaln_setup
+)
+
+
+def _adaln_setup(ctx, inputs, output):
+    z, _, scale, eps = inputs
+    ctx.save_for_backward(z, scale)
+    ctx.eps = eps
+
+
+def _adaln_backward(ctx, gh):
+    z, scale = ctx.saved_tensors
+    dz, dshift, dscale = _adaln_bwd_op(gh, z, scale, ctx.eps)
+    return dz, dshift, dscale, None
+
+
+torch.library.register_autograd("anima_flat_b200::adaln", _adaln_backward, setup_context=_adaln_setup)
 
 
 def _validate(x: torch.Tensor, *vecs: torch.Tensor) -> None:

@@ -16,7 +16,7 @@ from __future__ import annotations
 
 import torch
 
-from .._lib import call
+from .._lib import call, workspace
 from .common import BF16, _check, _check_dtype, _stream
 
 __all__ = ["head_norm", "qkv_norm_rope"]
@@ -96,6 +96,104 @@ def _head_norm(x: torch.Tensor, weight: torch.Tensor, heads: int, eps: float) ->
 @_head_norm.register_fake
 def _(x, weight, heads, eps):
     return x.new_empty((x.shape[0], x.shape[1], heads, weight.numel()))
+
+
+# ------------------------------------------------------------------ backward --
+# rope.py:443-613.  Weight gradients are reduced over all tokens and heads in a
+# fixed order (see csrc/headnorm_bwd.cu).
+@torch.library.custom_op("anima_flat_b200::head_norm_bwd", mutates_args=())
+def _head_norm_bwd_op(
+    x: torch.Tensor, dy: torch.Tensor, weight: torch.Tensor, heads: int, eps: float
+) -> tuple[torch.Tensor, torch.Tensor]:
+    B, S, _ = x.shape
+    hd = weight.numel()
+    dy = dy.contiguous()
+    dx = torch.empty_like(x)
+    dw = torch.empty(hd, dtype=F32, device=x.device)
+    ws, nbytes = workspace("afb_head_norm_bwd", x.device, B, S, heads, hd)
+    call(
+        "afb_head_norm_bwd",
+        x.data_ptr(), dy.data_ptr(), weight.data_ptr(), dx.data_ptr(), dw.data_ptr(),
+        B, S, heads, hd, eps, ws.data_ptr(), nbytes, _stream(x),
+    )
+    return dx, dw.to(weight.dtype)
+
+
+@_head_norm_bwd_op.register_fake
+def _(x, dy, weight, heads, eps):
+    return torch.empty_like(x), torch.empty_like(weight)
+
+
+def _head_norm_setup(ctx, inputs, output):
+    x, weight, heads, eps = inputs
+    ctx.save_for_backward(x, weight)
+    ctx.heads = heads
+    ctx.eps = eps
+
+
+def _head_norm_backward(ctx, dy):
+    x, weight = ctx.saved_tensors
+    dx, dw = _head_norm_bwd_op(x, dy, weight, ctx.heads, ctx.eps)
+    return dx, dw, None, None
+
+
+torch.library.register_autograd(
+    "anima_flat_b200::head_norm", _head_norm_backward, setup_context=_head_norm_setup
+)
+
+
+@torch.library.custom_op("anima_flat_b200::qkv_norm_rope_bwd", mutates_args=())
+def _qkv_norm_rope_bwd_op(
+    qkv: torch.Tensor,
+    dq: torch.Tensor,
+    dk: torch.Tensor,
+    dv: torch.Tensor,
+    q_weight: torch.Tensor,
+    k_weight: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    heads: int,
+    eps: float,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    B, S, _ = qkv.shape
+    hd = 2 * cos.shape[1]
+    dq, dk, dv = dq.contiguous(), dk.contiguous(), dv.contiguous()
+    dqkv = torch.empty_like(qkv)
+    dqw = torch.empty(hd, dtype=F32, device=qkv.device)
+    dkw = torch.empty(hd, dtype=F32, device=qkv.device)
+    ws, nbytes = workspace("afb_qkv_norm_rope_bwd", qkv.device, B, S, heads, hd)
+    call(
+        "afb_qkv_norm_rope_bwd",
+        qkv.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), q_weight.data_ptr(),
+        k_weight.data_ptr(), cos.data_ptr(), sin.data_ptr(), dqkv.data_ptr(), dqw.data_ptr(),
+        dkw.data_ptr(), B, S, heads, hd, eps, ws.data_ptr(), nbytes, _stream(qkv),
+    )
+    return dqkv, dqw.to(q_weight.dtype), dkw.to(k_weight.dtype)
+
+
+@_qkv_norm_rope_bwd_op.register_fake
+def _(qkv, dq, dk, dv, q_weight, k_weight, cos, sin, heads, eps):
+    return torch.empty_like(qkv), torch.empty_like(q_weight), torch.empty_like(k_weight)
+
+
+def _qkv_norm_rope_setup(ctx, inputs, output):
+    qkv, q_weight, k_weight, cos, sin, heads, eps = inputs
+    ctx.save_for_backward(qkv, q_weight, k_weight, cos, sin)
+    ctx.heads = heads
+    ctx.eps = eps
+
+
+def _qkv_norm_rope_backward(ctx, dq, dk, dv):
+    qkv, q_weight, k_weight, cos, sin = ctx.saved_tensors
+    dqkv, dqw, dkw = _qkv_norm_rope_bwd_op(
+        qkv, dq, dk, dv, q_weight, k_weight, cos, sin, ctx.heads, ctx.eps
+    )
+    return dqkv, dqw, dkw, None, None, None, None
+
+
+torch.library.register_autograd(
+    "anima_flat_b200::qkv_norm_rope_v", _qkv_norm_rope_backward, setup_context=_qkv_norm_rope_setup
+)
 
 
 def _f32(w: torch.Tensor) -> torch.Tensor:

@@ -563,6 +563,102 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------- per-op table --
+PER_OPS = ["residual_adaln", "adaln", "qkv_norm_rope", "head_norm", "residual_adaln_fp8",
+           "adaln_fp8", "rowquant", "rowquant_gelu"]
+
+
+def run_per_op(args):
+    """Each op alone at its config shape (config 2 for the bf16 ops, config 3
+    B=2 for the FP8 ops), inputs rotated over enough buffers to exceed 2x L2.
+    Prints one JSON line per op: stream time (back-to-back launches with PDL,
+    total / n) and isolated time (CUDA events around each launch)."""
+    import anima_flat_b200 as afb
+    from anima_flat_b200 import _lib
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    _lib.set_pdl(not args.no_pdl)
+    peak, peak_src = peak_hbm()
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    names = PER_OPS if args.op == "all" else args.op.split(",")
+    for name in names:
+        fp8 = name in ("residual_adaln_fp8", "adaln_fp8", "rowquant", "rowquant_gelu")
+        s = W.Shape(batch=2 if fp8 else 1)
+        B, S, D, H, hd = s.batch, s.seq, s.dim, s.heads, s.head_dim
+        g = torch.Generator(device=device).manual_seed(7)
+        act = lambda *d: torch.randn(*d, generator=g, device=device).to(torch.bfloat16)
+        vec = lambda: (0.1 * torch.randn(B, D, generator=g, device=device)).to(torch.bfloat16)
+        cos, sin = afb.rope_tables(64, 64, hd, device, (4.0, 4.0))
+        w = 1.0 + 0.02 * torch.randn(hd, generator=g, device=device)
+        nbytes = W.call_bytes(name, s)
+        nbuf = max(2, int(2 * l2 // max(1, nbytes)) + 1)
+        if name in ("residual_adaln", "residual_adaln_fp8"):
+            sets = [(act(B, S, D), act(B, S, D), vec(), vec(), vec() + 1) for _ in range(nbuf)]
+            fn = afb.residual_adaln if name == "residual_adaln" else afb.residual_adaln_fp8
+        elif name in ("adaln", "adaln_fp8"):
+            sets = [(act(B, S, D), vec(), vec() + 1) for _ in range(nbuf)]
+            fn = afb.adaln if name == "adaln" else afb.adaln_fp8
+        elif name == "qkv_norm_rope":
+            sets = [(act(B, S, 3 * H * hd), w, w, cos, sin, H) for _ in range(nbuf)]
+            fn = afb.qkv_norm_rope
+        elif name == "head_norm":
+            sets = [(act(B, S, H * hd), w, H) for _ in range(nbuf)]
+            fn = afb.head_norm
+        else:
+            K = s.mlp if name == "rowquant_gelu" else D
+            sets = [(act(B, S, K),) for _ in range(nbuf)]
+            fn = (lambda x: afb.rowquant(x, gelu=True)) if name == "rowquant_gelu" else afb.rowquant
+        n = max(args.steps, nbuf)
+        with torch.no_grad():
+            # stream: n launches back to back, captured in a graph
+            for i in range(max(args.warmup, 3)):
+                fn(*sets[i % nbuf])
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(n):
+                    fn(*sets[i % nbuf])
+            graph.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            us_stream = a.elapsed_time(b) * 1e3 / n
+            del graph
+            # isolated: external events around each launch inside a graph
+            # (no host gaps), PDL off so launches do not overlap
+            _lib.set_pdl(False)
+            ev = [(torch.cuda.Event(enable_timing=True, external=True),
+                   torch.cuda.Event(enable_timing=True, external=True)) for _ in range(n)]
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(n):
+                    ev[i][0].record()
+                    fn(*sets[i % nbuf])
+                    ev[i][1].record()
+            _lib.set_pdl(not args.no_pdl)
+            graph.replay()
+            torch.cuda.synchronize()
+            graph.replay()
+            torch.cuda.synchronize()
+            iso = sorted(x.elapsed_time(y) * 1e3 for x, y in ev)
+            us_iso = iso[len(iso) // 2]
+            del graph
+        print(json.dumps({
+            "op": name, "shape": {"batch": B, "seq": S, "dim": D, "heads": H, "head_dim": hd},
+            "bytes_per_launch": nbytes, "launches": n, "buffers": nbuf,
+            "us_stream": round(us_stream, 3), "gbs_stream": round(nbytes / us_stream / 1e3, 1),
+            "frac_stream": round(nbytes / us_stream / 1e3 / peak, 4),
+            "us_isolated_median": round(us_iso, 3), "gbs_isolated": round(nbytes / us_iso / 1e3, 1),
+            "frac_isolated": round(nbytes / us_iso / 1e3 / peak, 4),
+            "peak_gbs": peak, "peak_source": peak_src, "pdl": not args.no_pdl}), flush=True)
+        del sets
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -574,9 +670,14 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--op", default=None,
+                    help="per-op table instead of the step: 'all' or comma-separated op names")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_info()
+    if args.op:
+        run_per_op(args)
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
         return

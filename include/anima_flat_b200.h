@@ -113,6 +113,54 @@ int afb_head_norm(const void* x, const void* weight, void* y, int64_t batch,
                   int64_t seq, int64_t heads, int64_t head_dim, float eps,
                   void* stream);
 
+/* ----------------------------------------------------------------------- */
+/* Backward (LoRA training)                                                 */
+/* ----------------------------------------------------------------------- */
+/* Each backward entry point takes a caller-provided device workspace of at
+ * least the size its *_workspace query returns (fp32 partial sums of the
+ * parameter gradients); it is fully overwritten and needs no zeroing.  The
+ * parameter gradients are summed in a fixed order, so they are reproducible
+ * from run to run and across GPUs. */
+
+/* Replaces src/kernels/adaln.py:175-233 (_residual_adaln_bwd and the
+ * anima_flat::residual_adaln_bwd op, launching _residual_adaln_bwd_kernel,
+ * adaln.py:111-172).  gz may be NULL.  Outputs, in the op's order: dx, dres
+ * [batch, seq, dim]; dgate, dshift, dscale [batch, dim] bf16.  dim <= 2048. */
+size_t afb_residual_adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim);
+int afb_residual_adaln_bwd(const void* gh, const void* gz, const void* z, const void* x,
+                           const void* gate, const void* scale, void* dx, void* dres,
+                           void* dgate, void* dshift, void* dscale, int64_t batch,
+                           int64_t seq, int64_t dim, float eps, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Replaces src/kernels/adaln.py:247-252 (anima_flat::adaln_bwd, HAS_X=False,
+ * HAS_GZ=False): dz, dshift, dscale. */
+size_t afb_adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim);
+int afb_adaln_bwd(const void* gh, const void* z, const void* scale, void* dz, void* dshift,
+                  void* dscale, int64_t batch, int64_t seq, int64_t dim, float eps,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces src/kernels/rope.py:540-593 (_qkv_norm_rope_bwd and the
+ * anima_flat::qkv_norm_rope_bwd op, launching _qkv_norm_rope_bwd_kernel,
+ * rope.py:277-383).  dq, dk, dv: [batch, seq, heads, head_dim]; dqkv like
+ * qkv; dqw, dkw: [head_dim] fp32. */
+size_t afb_qkv_norm_rope_bwd_workspace(int64_t batch, int64_t seq, int64_t heads,
+                                       int64_t head_dim);
+int afb_qkv_norm_rope_bwd(const void* qkv, const void* dq, const void* dk, const void* dv,
+                          const void* q_weight, const void* k_weight, const void* cos,
+                          const void* sin, void* dqkv, void* dqw, void* dkw, int64_t batch,
+                          int64_t seq, int64_t heads, int64_t head_dim, float eps,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces src/kernels/rope.py:443-478 (_head_norm_bwd and the
+ * anima_flat::head_norm_bwd op, launching _head_norm_bwd_kernel,
+ * rope.py:386-436).  dx like x; dw: [head_dim] fp32. */
+size_t afb_head_norm_bwd_workspace(int64_t batch, int64_t seq, int64_t heads,
+                                   int64_t head_dim);
+int afb_head_norm_bwd(const void* x, const void* dy, const void* weight, void* dx, void* dw,
+                      int64_t batch, int64_t seq, int64_t heads, int64_t head_dim, float eps,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,6 +32,8 @@ def lib():
             "orc_canonical_sum": ([P, I, N], c_float),
             "orc_numpy_sum": ([P, I], c_float),
             "orc_f32_to_e4m3": ([c_float, N], ctypes.c_uint8),
+            "orc_adaln_bwd": ([P] * 11 + [I, I, I, F, N, N, N], None),
+            "orc_headnorm_bwd": ([P, I, I, I, I] + [P] * 10 + [I, I, I, I, F, N, N, N, N, N], None),
             "orc_e4m3_to_f32": ([ctypes.c_uint8], c_float),
         }
         for name, (args, res) in sigs.items():
@@ -133,3 +135,57 @@ def gelu(x_bits: np.ndarray) -> np.ndarray:
     y = np.empty(x.shape, np.float32)
     lib().orc_gelu_many(_p(x), _p(y), x.size)
     return y
+
+
+# Chunk geometry of the CUDA backward kernels (csrc/adaln_bwd.cu, headnorm_bwd.cu):
+# it fixes the order of the parameter-gradient sums.
+BWD_WARPS = 4
+BWD_ROWS_PER_WARP = 4
+HN_WARPS = 4
+HN_TOK_PER_WARP = 4
+
+
+def adaln_bwd(gh, z, scale, x=None, gate=None, gz=None, eps=1e-6, mode=RNE):
+    """Backward of (residual_)adaln.  Returns dict dz, dx, dgate, dshift, dscale."""
+    gh, z, scale = u16(gh), u16(z), u16(scale)
+    B, S, D = z.shape
+    has_x = x is not None
+    x = u16(x) if has_x else None
+    gate = u16(gate) if has_x else None
+    gz = u16(gz) if gz is not None else None
+    dz = np.empty((B, S, D), np.uint16)
+    dx = np.empty((B, S, D), np.uint16) if has_x else None
+    dgate = np.empty((B, D), np.uint16) if has_x else None
+    dshift = np.empty((B, D), np.uint16)
+    dscale = np.empty((B, D), np.uint16)
+    lib().orc_adaln_bwd(_p(gh), _p(gz), _p(z), _p(x), _p(gate), _p(scale), _p(dz), _p(dx),
+                        _p(dgate), _p(dshift), _p(dscale), B, S, D, eps, BWD_WARPS,
+                        BWD_ROWS_PER_WARP, mode)
+    return {"dz": dz, "dx": dx, "dgate": dgate, "dshift": dshift, "dscale": dscale}
+
+
+def qkv_norm_rope_bwd(qkv, dq, dk, dv, qw, kw, cos, sin, heads, eps=1e-5, mode=RNE):
+    qkv = u16(qkv)
+    B, S, W = qkv.shape
+    hd = W // (3 * heads)
+    width = heads * hd
+    dqkv = np.empty_like(qkv)
+    dqw = np.empty(hd, np.float32)
+    dkw = np.empty(hd, np.float32)
+    lib().orc_headnorm_bwd(_p(qkv), 3 * width, 0, width, 2 * width, _p(u16(dq)), _p(u16(dk)),
+                           _p(u16(dv)), _p(f32(qw)), _p(f32(kw)), _p(f32(cos)), _p(f32(sin)),
+                           _p(dqkv), _p(dqw), _p(dkw), B * S, S, heads, hd, eps, 1, 2, HN_WARPS,
+                           HN_TOK_PER_WARP, mode)
+    return dqkv, dqw, dkw
+
+
+def head_norm_bwd(x, dy, w, heads, eps=1e-5, mode=RNE):
+    x = u16(x)
+    B, S, W = x.shape
+    hd = W // heads
+    dx = np.empty_like(x)
+    dw = np.empty(hd, np.float32)
+    lib().orc_headnorm_bwd(_p(x), W, 0, 0, 0, _p(u16(dy)), None, None, _p(f32(w)), None, None,
+                           None, _p(dx), _p(dw), None, B * S, S, heads, hd, eps, 0, 1, HN_WARPS,
+                           HN_TOK_PER_WARP, mode)
+    return dx, dw

@@ -344,3 +344,161 @@ void orc_head_norm(const uint16_t* x, const float* w, uint16_t* y, int64_t B, in
                mode, buf);
   free(buf);
 }
+
+/* ------------------------------------------------------------ backward -- */
+
+/* src/kernels/adaln.py:133-217.  Per row: mean, rstd of z; xhat = d*rstd;
+ * dxh = gh*scale; c1 = sum(dxh)/D; c2 = sum(dxh*xhat)/D;
+ * dz = rstd*((dxh - c1) - xhat*c2) (+ gz) -> bf16; dx = bf16(dz*gate).
+ * Parameter gradients (dshift = sum gh, dscale = sum gh*xhat,
+ * dgate = sum dz*x) in the canonical order of the CUDA kernel: chunks of
+ * `warps * rows_per_warp` rows; in a chunk warp w sums rows w, w+warps, ...;
+ * the warp sums combine as a stride tree over warps (pairs w, w + warps/2
+ * first), the chunk sums add in increasing chunk order; then bf16.  In
+ * INTERP mode the per-row sums are numpy's; the parameter gradients keep the
+ * canonical order. */
+void orc_adaln_bwd(const uint16_t* gh, const uint16_t* gz, const uint16_t* z, const uint16_t* x,
+                   const uint16_t* gate, const uint16_t* scale, uint16_t* dz_out,
+                   uint16_t* dx_out, uint16_t* dgate, uint16_t* dshift, uint16_t* dscale,
+                   int64_t B, int64_t S, int64_t D, float eps, int warps, int rows_per_warp,
+                   int mode) {
+  const int has_x = x != NULL, nq = has_x ? 3 : 2;
+  const int64_t chunk_rows = (int64_t)warps * rows_per_warp;
+  const int64_t chunks = (S + chunk_rows - 1) / chunk_rows;
+  float* zf = (float*)malloc((size_t)D * sizeof(float));
+  float* t1 = (float*)malloc((size_t)D * sizeof(float));
+  float* t2 = (float*)malloc((size_t)D * sizeof(float));
+  float* wp = (float*)malloc((size_t)warps * nq * D * sizeof(float)); /* warp partials */
+  float* tot = (float*)malloc((size_t)nq * D * sizeof(float));
+  for (int64_t b = 0; b < B; ++b) {
+    const int64_t po = b * D;
+    for (int64_t i = 0; i < nq * D; ++i) tot[i] = 0.0f;
+    for (int64_t c = 0; c < chunks; ++c) {
+      for (int64_t i = 0; i < (int64_t)warps * nq * D; ++i) wp[i] = 0.0f;
+      for (int r = 0; r < rows_per_warp; ++r) {
+        for (int w = 0; w < warps; ++w) {
+          const int64_t s = c * chunk_rows + (int64_t)r * warps + w;
+          if (s >= S) continue;
+          const int64_t o = (b * S + s) * D;
+          for (int64_t i = 0; i < D; ++i) zf[i] = orc_bf16_to_f32(z[o + i]);
+          const float mean = row_sum(zf, D, 32, mode) / (float)D;
+          for (int64_t i = 0; i < D; ++i) {
+            const float d = zf[i] - mean;
+            t1[i] = d * d;
+          }
+          const float rstd = 1.0f / sqrtf(row_sum(t1, D, 32, mode) / (float)D + eps);
+          for (int64_t i = 0; i < D; ++i) {
+            const float xhat = (zf[i] - mean) * rstd;
+            const float dxh = orc_bf16_to_f32(gh[o + i]) * orc_bf16_to_f32(scale[po + i]);
+            t1[i] = dxh;
+            t2[i] = dxh * xhat;
+          }
+          const float c1 = row_sum(t1, D, 32, mode) / (float)D;
+          const float c2 = row_sum(t2, D, 32, mode) / (float)D;
+          float* p = wp + (int64_t)w * nq * D;
+          for (int64_t i = 0; i < D; ++i) {
+            const float g = orc_bf16_to_f32(gh[o + i]);
+            const float xhat = (zf[i] - mean) * rstd;
+            const float dxh = g * orc_bf16_to_f32(scale[po + i]);
+            float dz = rstd * ((dxh - c1) - xhat * c2);
+            if (gz) dz = dz + orc_bf16_to_f32(gz[o + i]);
+            dz_out[o + i] = orc_f32_to_bf16(dz, mode);
+            p[i] = p[i] + g;
+            p[D + i] = p[D + i] + g * xhat;
+            if (has_x) {
+              dx_out[o + i] = orc_f32_to_bf16(dz * orc_bf16_to_f32(gate[po + i]), mode);
+              p[2 * D + i] = p[2 * D + i] + dz * orc_bf16_to_f32(x[o + i]);
+            }
+          }
+        }
+      }
+      for (int span = warps; span > 1; span /= 2) /* stride tree over warps */
+        for (int w = 0; w < span / 2; ++w)
+          for (int64_t i = 0; i < nq * D; ++i)
+            wp[(int64_t)w * nq * D + i] = wp[(int64_t)w * nq * D + i] + wp[(int64_t)(w + span / 2) * nq * D + i];
+      for (int64_t i = 0; i < nq * D; ++i) tot[i] = tot[i] + wp[i];
+    }
+    for (int64_t i = 0; i < D; ++i) {
+      dshift[po + i] = orc_f32_to_bf16(tot[i], ROUND_RNE);
+      dscale[po + i] = orc_f32_to_bf16(tot[D + i], ROUND_RNE);
+      if (has_x) dgate[po + i] = orc_f32_to_bf16(tot[2 * D + i], ROUND_RNE);
+    }
+  }
+  free(zf); free(t1); free(t2); free(wp); free(tot);
+}
+
+/* src/kernels/rope.py:223-383, :386-436.  Per token and head: undo the
+ * rotation of the upstream gradient (da' = da*cos + db*sin,
+ * db' = db*cos - da*sin), rstd of the forward input, xhat = x*rstd,
+ * u = d'*w, c = sum(u*xhat)/hd, dx = bf16(rstd*(u - xhat*c)); dw += d'*xhat.
+ * Weight-gradient order as the CUDA kernel: tokens in chunks of
+ * warps * tok_per_warp, warp w takes tokens w, w+warps, ..., lane group g
+ * takes heads g, g + hpi, ... (hpi = 32 / (hd/8)); each (chunk, warp, group)
+ * slot sums sequentially from zero; slots add in increasing order.
+ * src/dsrc rows are src_row wide with the normed sections at q_off/k_off
+ * (nsec = 1 or 2) and, when dv is given, v at v_off. */
+void orc_headnorm_bwd(const uint16_t* src, int64_t src_row, int64_t q_off, int64_t k_off,
+                      int64_t v_off, const uint16_t* dq, const uint16_t* dk, const uint16_t* dv,
+                      const float* wq, const float* wk, const float* cs, const float* sn,
+                      uint16_t* dsrc, float* dw0, float* dw1, int64_t tokens, int64_t S,
+                      int64_t H, int64_t hd, float eps, int rotate, int nsec, int warps,
+                      int tok_per_warp, int mode) {
+  const int64_t half = hd / 2, lph = hd / 8, hpi = 32 / lph;
+  const int64_t chunk_toks = (int64_t)warps * tok_per_warp;
+  const int64_t chunks = (tokens + chunk_toks - 1) / chunk_toks;
+  float* x = (float*)malloc((size_t)hd * sizeof(float));
+  float* d = (float*)malloc((size_t)hd * sizeof(float));
+  float* t = (float*)malloc((size_t)hd * sizeof(float));
+  float* slot = (float*)malloc((size_t)2 * hd * sizeof(float));
+  float* tot = (float*)calloc((size_t)2 * hd, sizeof(float));
+  for (int64_t c = 0; c < chunks; ++c)
+    for (int w = 0; w < warps; ++w)
+      for (int64_t g = 0; g < hpi; ++g) {
+        for (int64_t i = 0; i < 2 * hd; ++i) slot[i] = 0.0f;
+        for (int r = 0; r < tok_per_warp; ++r) {
+          const int64_t tok = c * chunk_toks + (int64_t)r * warps + w;
+          if (tok >= tokens) continue;
+          const int64_t pos = tok % S;
+          for (int sec = 0; sec < nsec; ++sec) {
+            const uint16_t* in = src + tok * src_row + (sec ? k_off : q_off);
+            uint16_t* out = dsrc + tok * src_row + (sec ? k_off : q_off);
+            const uint16_t* go = (sec ? dk : dq) + tok * H * hd;
+            const float* wv = sec ? wk : wq;
+            for (int64_t h = g; h < H; h += hpi) {
+              for (int64_t i = 0; i < hd; ++i) {
+                x[i] = orc_bf16_to_f32(in[h * hd + i]);
+                d[i] = orc_bf16_to_f32(go[h * hd + i]);
+              }
+              if (rotate)
+                for (int64_t i = 0; i < half; ++i) {
+                  const float c0 = cs[pos * half + i], s0 = sn[pos * half + i];
+                  const float da = d[i], db = d[i + half];
+                  d[i] = (da * c0) + (db * s0);
+                  d[i + half] = (db * c0) - (da * s0);
+                }
+              for (int64_t i = 0; i < hd; ++i) t[i] = x[i] * x[i];
+              const float ss = (mode == ROUND_INTERP)
+                                   ? orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)
+                                   : orc_canonical_sum(t, hd, (int)lph);
+              const float rstd = 1.0f / sqrtf(ss / (float)hd + eps);
+              for (int64_t i = 0; i < hd; ++i) t[i] = (d[i] * wv[i]) * (x[i] * rstd);
+              const float cc = ((mode == ROUND_INTERP)
+                                    ? orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)
+                                    : orc_canonical_sum(t, hd, (int)lph)) / (float)hd;
+              for (int64_t i = 0; i < hd; ++i) {
+                const float xh = x[i] * rstd, u = d[i] * wv[i];
+                out[h * hd + i] = orc_f32_to_bf16(rstd * (u - xh * cc), mode);
+                slot[sec * hd + i] = slot[sec * hd + i] + d[i] * xh;
+              }
+            }
+          }
+          if (dv) memcpy(dsrc + tok * src_row + v_off, dv + tok * H * hd, (size_t)(H * hd) * 2);
+        }
+        for (int64_t i = 0; i < 2 * hd; ++i) tot[i] = tot[i] + slot[i];
+      }
+  for (int64_t i = 0; i < hd; ++i) {
+    dw0[i] = tot[i];
+    if (nsec > 1) dw1[i] = tot[hd + i];
+  }
+  free(x); free(d); free(t); free(slot); free(tot);
+}

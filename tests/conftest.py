@@ -54,11 +54,14 @@ def bf16_ulp(v: np.ndarray) -> np.ndarray:
     return 2.0 ** (e - 7)
 
 
-def ulp_diff_ok(ours_bits: np.ndarray, ref_f32: np.ndarray, ulps: float = 2.0) -> tuple[bool, float]:
-    """|ours - ref| <= ulps * bf16_ulp(ref) elementwise; returns (ok, worst ratio)."""
+def ulp_diff_ok(ours_bits: np.ndarray, ref_f32: np.ndarray, ulps: float = 2.0,
+                mag: np.ndarray | None = None) -> tuple[bool, float]:
+    """|ours - ref| <= ulps * bf16_ulp(m) elementwise, m = ref or the given
+    operand magnitude; returns (ok, worst ratio)."""
     ours = (ours_bits.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
     ref = ref_f32.astype(np.float64)
-    ratio = np.abs(ours - ref) / bf16_ulp(ref)
+    scale = np.maximum(np.abs(ref), np.abs(mag)) if mag is not None else ref
+    ratio = np.abs(ours - ref) / bf16_ulp(scale)
     worst = float(ratio.max()) if ratio.size else 0.0
     return worst <= ulps, worst
 

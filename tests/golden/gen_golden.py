@@ -141,6 +141,66 @@ def main() -> None:
         save(name, qkv=qkv, qw=qw, kw=kw, cos=cos, sin=sin, q=q, k=k, v=v, heads=np.int64(H),
              eps=np.float32(eps))
 
+    # --- backward (adaln.py:111-217, rope.py:277-577), partials summed as the
+    # reference's wrappers do ------------------------------------------------------
+    for name, (B, S, D, has_x, has_gz) in {
+        "residual_adaln_bwd_d2048": (2, 11, 2048, True, True),
+        "residual_adaln_bwd_nogz_d256": (1, 20, 256, True, False),
+        "adaln_bwd_d2048": (2, 9, 2048, False, False),
+    }.items():
+        rows = 8
+        nchunks = triton.cdiv(S, rows)
+        z = randn(B, S, D).to(bf)
+        x = randn(B, S, D).to(bf)
+        gh = randn(B, S, D, std=1e-2).to(bf)
+        gz = randn(B, S, D, std=1e-2).to(bf)
+        shift, scale, gate = mods(B, D)
+        dz = torch.empty_like(z)
+        dx = torch.empty_like(z)
+        part = lambda: torch.empty(B, nchunks, D, dtype=torch.float32)
+        psh, psc, pg = part(), part(), part()
+        A._residual_adaln_bwd_kernel.fn[(B, nchunks)](
+            gh, gz if has_gz else gh, z, x if has_x else z, gate if has_x else scale, scale, dz,
+            dx if has_x else dz, psh, psc, pg if has_x else psh, S, 1e-6, D=D,
+            BLOCK=triton.next_power_of_2(D), ROWS=rows, HAS_X=has_x, HAS_GZ=has_gz)
+        out = dict(gh=gh, z=z, scale=scale, dz=dz, dshift=psh.sum(1).to(bf), dscale=psc.sum(1).to(bf),
+                   eps=np.float32(1e-6))
+        if has_x:
+            out.update(x=x, gate=gate, dx=dx, dgate=pg.sum(1).to(bf))
+        if has_gz:
+            out.update(gz=gz)
+        save(name, **out)
+
+    B, hh, ww, H, hd, rows = 2, 3, 4, 5, 128, 8
+    S = hh * ww
+    cos, sin = rope_tables(hh, ww, hd, "cpu", (4.0, 4.0))
+    qkv = randn(B, S, 3 * H * hd).to(bf)
+    dq, dk, dv = (randn(B, S, H, hd, std=1e-2).to(bf) for _ in range(3))
+    qw = 1.0 + randn(hd, std=0.02)
+    kw = 1.0 + randn(hd, std=0.02)
+    hpp = min(4, triton.next_power_of_2(H))
+    gq = triton.cdiv(H, hpp)
+    chunks = B * triton.cdiv(S, rows)
+    dqkv = torch.empty_like(qkv)
+    pw = torch.empty(chunks, 3 * gq, hd, dtype=torch.float32)
+    R._qkv_norm_rope_bwd_kernel.fn[(chunks, 3 * gq)](
+        qkv, dq, dk, dv, dqkv, qw, kw, cos, sin, pw, S, 1e-5, HEADS=H, HALF=hd // 2, HPP=hpp,
+        ROWS=rows)
+    save("qkv_norm_rope_bwd_h5", qkv=qkv, dq=dq, dk=dk, dv=dv, qw=qw, kw=kw, cos=cos, sin=sin,
+         dqkv=dqkv, dqw=pw[:, :gq].sum((0, 1)), dkw=pw[:, gq:2 * gq].sum((0, 1)),
+         heads=np.int64(H), eps=np.float32(1e-5))
+
+    x = randn(B, S, H * hd).to(bf)
+    dy = randn(B, S, H, hd, std=1e-2).to(bf)
+    w = 1.0 + randn(hd, std=0.02)
+    groups = triton.cdiv(H, hpp)
+    dx = torch.empty_like(x)
+    pw = torch.empty(chunks, groups, hd, dtype=torch.float32)
+    R._head_norm_bwd_kernel.fn[(chunks, groups)](x, dy, dx, w, pw, S, 1e-5, HEADS=H,
+                                                 HALF=hd // 2, HPP=hpp, ROWS=rows)
+    save("head_norm_bwd_h5", x=x, dy=dy, w=w, dx=dx, dw=pw.sum((0, 1)), heads=np.int64(H),
+         eps=np.float32(1e-5))
+
     B, S, H, hd = 2, 5, 4, 128
     x = randn(B, S, H * hd).to(bf)
     w = 1.0 + randn(hd, std=0.02)

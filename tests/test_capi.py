@@ -32,7 +32,23 @@ def test_every_declared_symbol_is_exported(name):
 
 def test_signature_table_covers_compute_entry_points():
     utility = {"afb_abi_version", "afb_last_error", "afb_clear_error", "afb_set_pdl", "afb_get_pdl"}
-    assert set(HEADER_FUNCS) - utility == set(_lib.SIGNATURES)
+    assert set(HEADER_FUNCS) - utility == set(_lib.SIGNATURES) | set(_lib.WORKSPACE_QUERIES)
+
+
+def test_workspace_queries():
+    lib = _lib.load()
+    # [B][chunks of 16 rows][3][D] fp32
+    assert lib.afb_residual_adaln_bwd_workspace(1, 4096, 2048) == 1 * 256 * 3 * 2048 * 4
+    assert lib.afb_adaln_bwd_workspace(2, 17, 256) == 2 * 2 * 2 * 256 * 4
+    # [chunks of 16 tokens][4 warps][2 head groups][2][128] fp32
+    assert lib.afb_qkv_norm_rope_bwd_workspace(1, 4096, 16, 128) == 256 * 4 * 2 * 2 * 128 * 4
+    assert lib.afb_head_norm_bwd_workspace(1, 4096, 16, 128) == 256 * 4 * 2 * 1 * 128 * 4
+
+
+def test_backward_rejects_small_workspace():
+    rc, msg = _status("afb_adaln_bwd", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 32, 2048, 1e-6,
+                      FAKE, 16, None)
+    assert rc == 1 and "workspace too small" in msg
 
 
 def _status(name, *args):

@@ -193,16 +193,31 @@ def test_config2_within_2_ulp_of_torch_fp32(cuda_dev):
     h, z = afb.residual_adaln(*t)
     h_ref, z_ref = Fm.residual_adaln(*t)
     assert torch.equal(z, z_ref)
-    ok, worst = ulp_diff_ok(to_bits(h), Fm.adaln_y(z_ref, t[3], t[4], 1e-6).cpu().numpy())
+    # 2 bf16 ulp at the magnitude of the last addition's operands (LN(z)*scale
+    # and shift): where they cancel, the result itself is no measure of error.
+    t_ref = torch.nn.functional.layer_norm(z_ref.float(), (D,), eps=1e-6) * t[4].float()[:, None]
+    y_ref = t_ref + t[3].float()[:, None]
+    mag = torch.maximum(y_ref.abs(), torch.maximum(t_ref.abs(), t[3].float()[:, None].abs()))
+    ok, worst = ulp_diff_ok(to_bits(h), y_ref.cpu().numpy(), 2.0, mag=mag.cpu().numpy())
     assert ok, worst
+    strict = ulp_diff_ok(to_bits(h), y_ref.cpu().numpy(), 2.0)[1]
+    print(f"residual_adaln vs torch fp32: worst {worst:.3f} ulp (operand scale), {strict:.1f} ulp of y")
     qkv, qw, kw, cos, sin = qkv_inputs(r, B, S, H, hd)
     a = [from_bits(v, cuda_dev) for v in (qkv, qw, kw, cos, sin)]
     with torch.no_grad():
         q, k, _ = afb.qkv_norm_rope(*a, H, 1e-5)
-    qr, kr, _ = Fm.qkv_norm_rope(*a, H, 1e-5)
-    # rotation inputs are the bf16-rounded normed values; compare against fp32 rotation
-    assert (q.float() - qr.float()).abs().max() <= 2 * 2.0 ** -7 * qr.float().abs().max()
-    assert (k.float() - kr.float()).abs().max() <= 2 * 2.0 ** -7 * kr.float().abs().max()
+    # fp32 rotation of the torch-normed heads; tolerance at the rotation operands' scale
+    qkv_t = a[0].view(B, S, 3, H, hd)
+    for ours, part, w in ((q, qkv_t[:, :, 0], a[1]), (k, qkv_t[:, :, 1], a[2])):
+        n = Fm._rms_heads(part, w, 1e-5).float()
+        half = hd // 2
+        na, nb = n[..., :half], n[..., half:]
+        c, s_ = a[3][None, :, None, :], a[4][None, :, None, :]
+        y = torch.cat([na * c - nb * s_, nb * c + na * s_], dim=-1)
+        mag = torch.cat([torch.maximum((na * c).abs(), (nb * s_).abs()),
+                         torch.maximum((nb * c).abs(), (na * s_).abs())], dim=-1)
+        ok, worst = ulp_diff_ok(to_bits(ours), y.cpu().numpy(), 2.0, mag=mag.cpu().numpy())
+        assert ok, worst
 
 
 def test_pdl_off_gives_identical_results(cuda_dev):

@@ -226,3 +226,53 @@ def test_canonical_sum_definition():
     while p.size > 1:
         p = p[: p.size // 2] + p[p.size // 2:]
     assert C.canonical_sum(x, 32) == np.float32(p[0])
+
+
+# ----------------------------------------------------------------- backward --
+BWD_CASES = ["residual_adaln_bwd_d2048", "residual_adaln_bwd_nogz_d256", "adaln_bwd_d2048"]
+
+
+@pytest.mark.parametrize("name", BWD_CASES)
+def test_pin_adaln_bwd(name):
+    """Per-row grads bit-exact; bf16 parameter grads equal (the reference sums
+    its partials with torch, in another order; after bf16 rounding they agree)."""
+    g = golden(name)
+    o = C.adaln_bwd(g["gh"], g["z"], g["scale"], x=g.get("x"), gate=g.get("gate"), gz=g.get("gz"),
+                    eps=float(g["eps"]), mode=C.INTERP)
+    for k in ("dz", "dx", "dgate", "dshift", "dscale"):
+        if k in g:
+            np.testing.assert_array_equal(o[k], g[k], err_msg=k)
+
+
+def test_pin_qkv_norm_rope_bwd():
+    g = golden("qkv_norm_rope_bwd_h5")
+    d, a, b = C.qkv_norm_rope_bwd(g["qkv"], g["dq"], g["dk"], g["dv"], g["qw"], g["kw"], g["cos"],
+                                  g["sin"], int(g["heads"]), eps=float(g["eps"]), mode=C.INTERP)
+    np.testing.assert_array_equal(d, g["dqkv"])
+    np.testing.assert_allclose(a, g["dqw"], rtol=2e-5)
+    np.testing.assert_allclose(b, g["dkw"], rtol=2e-5)
+
+
+def test_pin_head_norm_bwd():
+    g = golden("head_norm_bwd_h5")
+    dx, dw = C.head_norm_bwd(g["x"], g["dy"], g["w"], int(g["heads"]), eps=float(g["eps"]),
+                             mode=C.INTERP)
+    np.testing.assert_array_equal(dx, g["dx"])
+    np.testing.assert_allclose(dw, g["dw"], rtol=2e-5)
+
+
+def test_formulation_adaln_bwd_matches_autograd():
+    """The canonical backward against torch autograd of the fp32 composition."""
+    g = golden("residual_adaln_bwd_d2048")
+    o = C.adaln_bwd(g["gh"], g["z"], g["scale"], x=g["x"], gate=g["gate"], gz=g["gz"],
+                    eps=float(g["eps"]))
+    z = _t(g["z"]).float().requires_grad_(True)
+    sc = _t(g["scale"]).float().requires_grad_(True)
+    sh = torch.zeros_like(sc, requires_grad=True)
+    y = torch.nn.functional.layer_norm(z, (z.shape[-1],), eps=1e-6) * sc[:, None] + sh[:, None]
+    y.backward(_t(g["gh"]).float())
+    dz_ref = z.grad + _t(g["gz"]).float()
+    dz = (o["dz"].astype(np.uint32) << 16).view(np.float32)
+    assert np.abs(dz - dz_ref.numpy()).max() <= 2 * 2.0 ** -8 * np.abs(dz_ref.numpy()).max()
+    dsc = (o["dscale"].astype(np.uint32) << 16).view(np.float32)
+    assert np.abs(dsc - sc.grad.numpy()).max() <= 2 * 2.0 ** -8 * np.abs(sc.grad.numpy()).max()
