@@ -8,13 +8,15 @@
 //   canonical_sum(x[0..n), P):      n = 8*NV, NVp = max(P, pow2ceil(NV)),
 //     vectors X[v] = x[8v .. 8v+8) (zero for v >= NV);
 //     while NVp > P:  X[v] += X[v + NVp/2]  (v < NVp/2, elementwise);
-//     p[v] = ((X0+X1)+(X2+X3)) + ((X4+X5)+(X6+X7))   for v < P;
+//     p[v] = ((X0+X4)+(X2+X6)) + ((X1+X5)+(X3+X7))   for v < P;
 //     while P > 1:    p[v] += p[v + P/2];
 //     result p[0].
 //
-// A warp that keeps vector v = lane + 32*c in lane `lane` realises it exactly:
-// an in-lane stride tree over c, the intra-vector tree, then an xor butterfly
-// (strides 16..1), which pairs the same operands (addition commutes exactly).
+// (the intra-vector step is itself a stride tree, so that it maps onto packed
+// fp32x2 adds).  A warp that keeps vector v = lane + 32*c in lane `lane`
+// realises it exactly: an in-lane stride tree over c, the intra-vector tree,
+// then an xor butterfly (strides 16..1), which pairs the same operands
+// (addition commutes exactly).
 // Every other operation is a single IEEE-754 fp32 operation (no contraction:
 // the library is built with --fmad=false and uses __f*_rn intrinsics), bf16
 // rounding is round-to-nearest-even, FP8 e4m3 rounding is RNE with
@@ -126,8 +128,8 @@ __device__ __forceinline__ uint2 e4m3x8(const float (&f)[8]) {
 // Canonical sums.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float vec_sum8(const float (&f)[8]) {
-  return __fadd_rn(__fadd_rn(__fadd_rn(f[0], f[1]), __fadd_rn(f[2], f[3])),
-                   __fadd_rn(__fadd_rn(f[4], f[5]), __fadd_rn(f[6], f[7])));
+  return __fadd_rn(__fadd_rn(__fadd_rn(f[0], f[4]), __fadd_rn(f[2], f[6])),
+                   __fadd_rn(__fadd_rn(f[1], f[5]), __fadd_rn(f[3], f[7])));
 }
 
 // Warp-wide canonical sum (P = 32) of the vectors a lane holds at
@@ -187,6 +189,159 @@ __device__ __forceinline__ float warp_max(float v) {
 // 1 / sqrt(v + eps) with two IEEE roundings (no rsqrt approximation).
 __device__ __forceinline__ float canonical_rstd(float var, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
+// ---------------------------------------------------------------------------
+// Bulk asynchronous copies (TMA engine, non-tensor form) into shared memory,
+// completing on an mbarrier.  No cluster multicast is used anywhere.
+// ---------------------------------------------------------------------------
+// Device-side status word of this translation unit: set when a bounded wait
+// gives up (never expected).  Each .cu file that waits reports it through its
+// own host reader (afb::read_status_* in afb_launch.h).
+static __device__ int g_afb_device_status = 0;
+constexpr int kStatusWaitTimeout = 1;
+// try_wait suspends for a hardware-defined interval per call; this bounds a
+// wait to far beyond any real copy latency (seconds), then reports failure.
+constexpr uint32_t kMaxWaitSpins = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+// Make barrier initialisation visible to the async proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Order this thread's prior generic-proxy shared-memory accesses before later
+// async-proxy (bulk copy) writes to the same buffer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+// global -> shared bulk copy of `bytes` (multiple of 16, both ends 16-byte
+// aligned), signalling `bar` with complete_tx.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// Wait for the phase of `bar` with the given parity to complete; false (and the
+// device status set) if the bound is exhausted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMaxWaitSpins; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  atomicOr(&g_afb_device_status, kStatusWaitTimeout);
+  return false;
+}
+__device__ __forceinline__ uint4 lds16(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+// ---------------------------------------------------------------------------
+// Packed arithmetic.  Blackwell executes two IEEE fp32 operations per
+// instruction on a 64-bit register pair (add/sub/mul.rn.f32x2), and bf16x2
+// multiply/add round the exact result once (RNE).  For bf16 operands,
+// add.rn.bf16x2(res, mul.rn.bf16x2(g, x)) equals bf16(fp32(res + bf16(g*x))):
+// g*x of two bf16 is exact in fp32, and when res and the product are 17 or
+// more binades apart the fp32 sum rounds to res's bf16 neighbourhood either
+// way, so the double rounding of the fp32 route never differs.
+// ---------------------------------------------------------------------------
+typedef unsigned long long f2_t;  // two fp32 lanes {lo, hi}
+
+__device__ __forceinline__ f2_t f2(float lo, float hi) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float f2lo(f2_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2hi(f2_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ f2_t add2(f2_t a, f2_t b) {
+  f2_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2_t sub2(f2_t a, f2_t b) {
+  f2_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
+  f2_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// bf16 pair (packed in one 32-bit word) -> fp32 pair.
+__device__ __forceinline__ f2_t bf2f2(uint32_t w) { return f2(bf_lo(w), bf_hi(w)); }
+// fp32 pair -> bf16 pair, round to nearest even.
+__device__ __forceinline__ uint32_t f2bf2(f2_t v) { return pack2_rn(f2lo(v), f2hi(v)); }
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t word(const uint4 v, int j) {
+  return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+}
+
+// Canonical warp sum (P = 32) of the 8-element vectors a lane holds at
+// v = lane + 32*c, given as packed pairs p[c][j] = elements (2j, 2j+1).
+// Consumes p.  Same operations as warp_canonical_sum.
+template <int NC>
+__device__ __forceinline__ float warp_canonical_sum2(f2_t (&p)[NC][4]) {
+#pragma unroll
+  for (int s = NC / 2; s >= 1; s >>= 1) {
+#pragma unroll
+    for (int c = 0; c < s; ++c) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[c][j] = add2(p[c][j], p[c + s][j]);
+    }
+  }
+  // intra-vector stride tree: (e0+e4, e1+e5), (e2+e6, e3+e7), then pairs, then halves
+  const f2_t q = add2(add2(p[0][0], p[0][2]), add2(p[0][1], p[0][3]));
+  float r = __fadd_rn(f2lo(q), f2hi(q));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) r = __fadd_rn(r, __shfl_xor_sync(kFull, r, o));
+  return r;
+}
+
+// The same with the pairs produced on demand by val(c, j); the first stride
+// level is formed from val directly.
+template <int NC, typename F>
+__device__ __forceinline__ float warp_canonical_sum2_fn(F val) {
+  constexpr int H = NC > 1 ? NC / 2 : 1;
+  f2_t p[H][4];
+#pragma unroll
+  for (int c = 0; c < H; ++c) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (NC > 1) {
+        p[c][j] = add2(val(c, j), val(c + H, j));
+      } else {
+        p[c][j] = val(c, j);
+      }
+    }
+  }
+  return warp_canonical_sum2<H>(p);
 }
 
 // ---------------------------------------------------------------------------

@@ -17,8 +17,26 @@ constexpr int kRowWarps = 4;
 // Largest row width the warp-per-row kernels hold in registers.
 constexpr int64_t kMaxRowDim = 4096;
 
+// Properties of the current device, read once per device.
+struct DeviceInfo {
+  int sms = 0;
+  size_t max_smem_optin = 0;  // dynamic shared memory a CTA may opt into
+  cudaError_t error = cudaSuccess;
+};
+const DeviceInfo& device_info();
+
+// Opt a kernel into `bytes` of dynamic shared memory (cached per kernel).
+cudaError_t ensure_smem_raw(const void* kernel, size_t bytes);
+template <typename K>
+cudaError_t ensure_smem(K kernel, size_t bytes) {
+  return ensure_smem_raw(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 // Set by afb_set_pdl(); defaults to on unless AFB_PDL=0 is in the environment.
 bool pdl_enabled();
+
+// Host readers of the per-file device status words (OR-ed by afb_device_status).
+cudaError_t read_status_adaln_fwd(int* status);
 
 // Records `msg` as this thread's last error (read by afb_last_error()).
 void set_error(const std::string& msg);

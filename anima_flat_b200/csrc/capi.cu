@@ -1,7 +1,10 @@
 // Library-wide C-ABI entry points: version, last error, PDL switch.
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 
 #include "afb_launch.h"
 
@@ -15,6 +18,44 @@ int g_pdl = -1;  // -1: read AFB_PDL from the environment on first use
 void set_error(const std::string& msg) { g_last_error = msg; }
 const std::string& last_error() { return g_last_error; }
 
+const DeviceInfo& device_info() {
+  static std::mutex mu;
+  static std::map<int, DeviceInfo> cache;
+  int dev = 0;
+  DeviceInfo bad;
+  bad.error = cudaGetDevice(&dev);
+  if (bad.error != cudaSuccess) {
+    static thread_local DeviceInfo err;
+    err = bad;
+    return err;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  DeviceInfo info;
+  int smem = 0;
+  info.error = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev);
+  if (info.error == cudaSuccess)
+    info.error = cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  info.max_smem_optin = static_cast<size_t>(smem);
+  return cache.emplace(dev, info).first->second;
+}
+
+cudaError_t ensure_smem_raw(const void* kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& have = done[{dev, kernel}];
+  if (have >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(bytes));
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
+
 bool pdl_enabled() {
   if (g_pdl < 0) {
     const char* env = std::getenv("AFB_PDL");
@@ -26,6 +67,19 @@ bool pdl_enabled() {
 }  // namespace afb
 
 extern "C" int afb_abi_version(void) { return 1; }
+
+// Device status word of the current device (0: no bounded wait ever gave up).
+extern "C" int afb_device_status(int* status) {
+  int v = 0, all = 0;
+  cudaError_t e = afb::read_status_adaln_fwd(&v);
+  all |= v;
+  if (e != cudaSuccess) {
+    afb::set_error(std::string("afb_device_status: ") + cudaGetErrorString(e));
+    return static_cast<int>(e);
+  }
+  *status = all;
+  return 0;
+}
 
 extern "C" const char* afb_last_error(void) { return afb::g_last_error.c_str(); }
 

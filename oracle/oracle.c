@@ -97,7 +97,8 @@ float orc_e4m3_to_f32(uint8_t b) {
 /* Sum of x[0..n) (n a multiple of 8) in the canonical order: zero-pad to
  * NVp = max(P, pow2ceil(n/8)) vectors of 8; halve the vector count by adding
  * vector v + NVp/2 into vector v until P remain; reduce each remaining vector
- * as ((x0+x1)+(x2+x3))+((x4+x5)+(x6+x7)); halve the P partials the same way. */
+ * by the same stride rule, ((x0+x4)+(x2+x6))+((x1+x5)+(x3+x7)); halve the P
+ * partials the same way. */
 float orc_canonical_sum(const float* x, int64_t n, int P) {
   int64_t nv = n / 8, nvp = P;
   while (nvp < nv) nvp <<= 1;
@@ -112,7 +113,7 @@ float orc_canonical_sum(const float* x, int64_t n, int P) {
   float* p = (float*)malloc((size_t)P * sizeof(float));
   for (int v = 0; v < P; ++v) {
     const float* q = X + (int64_t)v * 8;
-    p[v] = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
+    p[v] = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
   }
   for (int w = P; w > 1; w /= 2)
     for (int v = 0; v < w / 2; ++v) p[v] = p[v] + p[v + w / 2];

@@ -219,10 +219,10 @@ def test_bf16_rounding_matches_torch():
 def test_canonical_sum_definition():
     """The canonical order on a small case, spelled out by hand."""
     x = np.arange(1, 513, dtype=np.float32) * np.float32(0.1)
-    # 64 vectors -> stride tree to 32 -> intra-vector tree -> stride tree over 32.
+    # 64 vectors -> stride tree to 32 -> intra-vector stride tree -> stride tree over 32.
     X = x.reshape(64, 8)
     X = X[:32] + X[32:]
-    p = ((X[:, 0] + X[:, 1]) + (X[:, 2] + X[:, 3])) + ((X[:, 4] + X[:, 5]) + (X[:, 6] + X[:, 7]))
+    p = ((X[:, 0] + X[:, 4]) + (X[:, 2] + X[:, 6])) + ((X[:, 1] + X[:, 5]) + (X[:, 3] + X[:, 7]))
     while p.size > 1:
         p = p[: p.size // 2] + p[p.size // 2:]
     assert C.canonical_sum(x, 32) == np.float32(p[0])
