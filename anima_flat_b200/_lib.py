@@ -79,6 +79,8 @@ def load() -> ctypes.CDLL:
     lib.afb_abi_version.argtypes = []
     lib.afb_last_error.restype = ctypes.c_char_p
     lib.afb_last_error.argtypes = []
+    lib.afb_device_status.argtypes = [ctypes.POINTER(c_int)]
+    lib.afb_device_status.restype = c_int
     lib.afb_set_pdl.argtypes = [c_int]
     lib.afb_set_pdl.restype = None
     lib.afb_get_pdl.argtypes = []

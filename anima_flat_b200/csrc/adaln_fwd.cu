@@ -18,7 +18,8 @@
 // computes.  A row moves from its stage into registers (lane l holds the
 // 16-byte vectors v = l + 32*c, c < NC), the stage is refilled at once, and
 // z and h (or q) are written straight from registers.  z = res + gate*x uses
-// packed bf16x2 arithmetic, the statistics and the modulation packed fp32x2.
+// packed bf16x2 arithmetic; the statistics and the modulation use packed
+// fp32x2 adds/subs under the contraction rule of afb_device.cuh.
 #include "afb_device.cuh"
 #include "afb_launch.h"
 
@@ -131,7 +132,7 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw) {
     const f2_t mm = f2(mean, mean);
     const float var = __fdiv_rn(warp_canonical_sum2_fn<NC>([&](int c, int jj) {
                                   const f2_t d = ok(c) ? sub2(bf2f2(word(zv[c], jj)), mm) : 0ull;
-                                  return mul2(d, d);
+                                  return mul2_noc(d, d);
                                 }),
                                 fd);
     const float rstd = canonical_rstd(var, a.eps);
@@ -139,7 +140,7 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw) {
     // y = ((z - mean) * rstd) * scale + shift for elements (2jj, 2jj+1) of vector c
     auto ypair = [&](int c, int jj, const uint4& scv, const uint4& shv) {
       const f2_t d = sub2(bf2f2(word(zv[c], jj)), mm);
-      return add2(mul2(mul2(d, rr), bf2f2(word(scv, jj))), bf2f2(word(shv, jj)));
+      return add2(mul2_noc(mul2(d, rr), bf2f2(word(scv, jj))), bf2f2(word(shv, jj)));
     };
 
     if (!FP8) {

@@ -255,7 +255,16 @@ __device__ __forceinline__ uint4 lds16(const void* p) {
 // ---------------------------------------------------------------------------
 // Packed arithmetic.  Blackwell executes two IEEE fp32 operations per
 // instruction on a 64-bit register pair (add/sub/mul.rn.f32x2), and bf16x2
-// multiply/add round the exact result once (RNE).  For bf16 operands,
+// multiply/add round the exact result once (RNE).
+//
+// Contraction rule.  With CUDA 12.9's ptxas, a mul.rn.f32x2 whose result
+// feeds an add.rn.f32x2 can come out fused into one packed FMA (observed on
+// B200: sums of packed squares differed by an ulp in ~9% of rows; exact with
+// ptxas -O0, unchanged by -fmad=false).  Scalar mul.rn.f32 is never fused.
+// So packed f32x2 is used only for adds/subs, for a sub feeding a multiply
+// and for a multiply feeding a multiply; every product that is then added
+// (squares in the variance, the scale product before + shift) is formed with
+// scalar __fmul_rn.  For bf16 operands,
 // add.rn.bf16x2(res, mul.rn.bf16x2(g, x)) equals bf16(fp32(res + bf16(g*x))):
 // g*x of two bf16 is exact in fp32, and when res and the product are 17 or
 // more binades apart the fp32 sum rounds to res's bf16 neighbourhood either
@@ -280,6 +289,8 @@ __device__ __forceinline__ f2_t sub2(f2_t a, f2_t b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+// Packed multiply: only where the result feeds another multiply or is rounded
+// directly (see the contraction rule above).
 __device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
   f2_t r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -289,6 +300,11 @@ __device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
 __device__ __forceinline__ f2_t bf2f2(uint32_t w) { return f2(bf_lo(w), bf_hi(w)); }
 // fp32 pair -> bf16 pair, round to nearest even.
 __device__ __forceinline__ uint32_t f2bf2(f2_t v) { return pack2_rn(f2lo(v), f2hi(v)); }
+// Element-wise scalar products of two pairs, kept scalar so that they are never
+// contracted into a following add.
+__device__ __forceinline__ f2_t mul2_noc(f2_t a, f2_t b) {
+  return f2(__fmul_rn(f2lo(a), f2lo(b)), __fmul_rn(f2hi(a), f2hi(b)));
+}
 __device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));

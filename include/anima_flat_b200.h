@@ -35,6 +35,11 @@ int afb_abi_version(void);
 const char* afb_last_error(void);
 void afb_clear_error(void);
 
+/* Device status of the current device: 0, or a bit set by a kernel whose
+ * bounded wait on an asynchronous copy gave up (then the kernel stopped
+ * early and its outputs are incomplete).  No reference counterpart. */
+int afb_device_status(int* status);
+
 /* Programmatic dependent launch on (1, default) or off (0).  Also read from
  * the environment variable AFB_PDL=0 at first use. */
 void afb_set_pdl(int enabled);

@@ -31,7 +31,8 @@ def test_every_declared_symbol_is_exported(name):
 
 
 def test_signature_table_covers_compute_entry_points():
-    utility = {"afb_abi_version", "afb_last_error", "afb_clear_error", "afb_set_pdl", "afb_get_pdl"}
+    utility = {"afb_abi_version", "afb_last_error", "afb_clear_error", "afb_set_pdl", "afb_get_pdl",
+               "afb_device_status"}
     assert set(HEADER_FUNCS) - utility == set(_lib.SIGNATURES) | set(_lib.WORKSPACE_QUERIES)
 
 
