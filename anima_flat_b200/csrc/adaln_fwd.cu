@@ -126,15 +126,17 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw) {
     }
 
     // Statistics (canonical order, see afb_device.cuh), packed fp32x2.
-    const float fd = static_cast<float>(D);
-    const float mean = __fdiv_rn(
-        warp_canonical_sum2_fn<NC>([&](int c, int jj) { return bf2f2(word(zv[c], jj)); }), fd);
+    // x / D; for EXACT, D = 256 * NC is a power of two and x * (1/D) rounds identically
+    auto div_d = [&](float x) {
+      return EXACT ? __fmul_rn(x, 1.0f / (NC * 256)) : __fdiv_rn(x, static_cast<float>(D));
+    };
+    const float mean = div_d(
+        warp_canonical_sum2_fn<NC>([&](int c, int jj) { return bf2f2(word(zv[c], jj)); }));
     const f2_t mm = f2(mean, mean);
-    const float var = __fdiv_rn(warp_canonical_sum2_fn<NC>([&](int c, int jj) {
-                                  const f2_t d = ok(c) ? sub2(bf2f2(word(zv[c], jj)), mm) : 0ull;
-                                  return mul2_noc(d, d);
-                                }),
-                                fd);
+    const float var = div_d(warp_canonical_sum2_fn<NC>([&](int c, int jj) {
+      const f2_t d = ok(c) ? sub2(bf2f2(word(zv[c], jj)), mm) : 0ull;
+      return mul2_noc(d, d);
+    }));
     const float rstd = canonical_rstd(var, a.eps);
     const f2_t rr = f2(rstd, rstd);
     // y = ((z - mean) * rstd) * scale + shift for elements (2jj, 2jj+1) of vector c

@@ -37,6 +37,7 @@ bool pdl_enabled();
 
 // Host readers of the per-file device status words (OR-ed by afb_device_status).
 cudaError_t read_status_adaln_fwd(int* status);
+cudaError_t read_status_headnorm_fwd(int* status);
 
 // Records `msg` as this thread's last error (read by afb_last_error()).
 void set_error(const std::string& msg);

@@ -73,6 +73,10 @@ extern "C" int afb_device_status(int* status) {
   int v = 0, all = 0;
   cudaError_t e = afb::read_status_adaln_fwd(&v);
   all |= v;
+  if (e == cudaSuccess) {
+    e = afb::read_status_headnorm_fwd(&v);
+    all |= v;
+  }
   if (e != cudaSuccess) {
     afb::set_error(std::string("afb_device_status: ") + cudaGetErrorString(e));
     return static_cast<int>(e);

@@ -19,8 +19,9 @@ CUDA graph and launched with programmatic dependent launch.
 value: algorithmic HBM bytes of all ranks' steps / max-over-ranks device
 time (CUDA events), in GB/s.  e2e: the same metric through the public API
 with pinned host buffers, host<->device copies inside the timed region.
-roofline: the dominant kernel (residual_adaln) timed per launch with CUDA
-events recorded inside an instrumented copy of the step graph.
+roofline: the dominant kernel (residual_adaln): the step's 84 launches of it
+replayed alone back to back, CUDA events around the replays; the isolated
+per-launch time (events around each launch, no overlap) is reported beside it.
 cpu_baseline: the reference's unfused torch fp32 eager composition on the
 host cores (rank 0, N=1), on a bounded sample (config-1 shapes).
 
@@ -151,8 +152,11 @@ class Step:
             self.up = [act(B, S, s.mlp) for _ in range(L)]
         self.timed = "residual_adaln_fp8" if fp8 else "residual_adaln"
         self.timed_hook = None  # called around launches of self.timed when instrumenting
+        self.only = None  # run only the launches of this op (roofline timing)
 
     def _op(self, name, fn, *a, **kw):
+        if self.only is not None and name != self.only:
+            return None
         hook = self.timed_hook if name == self.timed else None
         if hook is not None:
             hook(True)
@@ -210,8 +214,17 @@ class Step:
                *self.block_mods(L, 2))
 
 
-def capture(step: Step):
-    """CUDA graph of one step (its outputs live in the graph's memory pool)."""
+def capture(step: Step, only: str | None = None):
+    """CUDA graph of one step (its outputs live in the graph's memory pool);
+    with `only`, just that op's launches of the step."""
+    step.only = only
+    try:
+        return _capture(step)
+    finally:
+        step.only = None
+
+
+def _capture(step: Step):
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
@@ -307,19 +320,32 @@ def run_ours(args, world, rank, local):
     rows_total = shape.rows * world * args.steps
     del g
 
-    # --- dominant kernel, per launch (instrumented graph, same K) ----------
+    # --- dominant kernel: the step's launches of it alone, back to back ---
     dominant = step.timed
-    g2, evs = instrumented_capture(step)
-    per_launch = []
-    for _ in range(max(3, args.warmup)):
+    n_dom = step.calls.count(dominant)
+    g2 = capture(step, only=dominant)
+    for _ in range(args.warmup):
         g2.replay()
     torch.cuda.synchronize()
+    t0.record()
     for _ in range(args.steps):
         g2.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    avg_ms = t0.elapsed_time(t1) / (args.steps * n_dom)
+    del g2
+    # and each launch on its own (events around every launch, no overlap)
+    g3, evs = instrumented_capture(step)
+    per_launch = []
+    for _ in range(max(3, args.warmup)):
+        g3.replay()
+    torch.cuda.synchronize()
+    for _ in range(min(args.steps, 10)):
+        g3.replay()
         torch.cuda.synchronize()
         per_launch += [a.elapsed_time(b) for a, b in evs]
-    del g2
-    avg_ms = sum(per_launch) / len(per_launch)
+    del g3
+    iso_ms = sorted(per_launch)[len(per_launch) // 2]
     dom_bytes = W.call_bytes(dominant, shape)
     achieved = dom_bytes / (avg_ms * 1e-3) / 1e9
     peak, peak_src = peak_hbm()
@@ -374,7 +400,11 @@ def run_ours(args, world, rank, local):
             "traffic": traffic,
             "bytes_per_launch": dom_bytes,
             "avg_launch_us": round(avg_ms * 1e3, 3),
-            "launches_timed": len(per_launch),
+            "launches_timed": args.steps * n_dom,
+            "timing": "the step's launches of this kernel alone, back to back (PDL), CUDA events "
+                      "around K graph replays",
+            "isolated_launch_us_median": round(iso_ms * 1e3, 3),
+            "isolated_frac": round(dom_bytes / (iso_ms * 1e-3) / 1e9 / peak, 4),
         },
         "clocks": clocks,
         "e2e": e2e,
