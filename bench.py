@@ -46,6 +46,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 from anima_flat_b200 import workload as W  # noqa: E402
+from anima_flat_b200.shard import max_over_ranks, shard_sequences  # noqa: E402
 
 METRIC = "fused AdaLN/RMSNorm/RoPE HBM GB/s"
 FALLBACK_HBM_GBS = 6650.0
@@ -116,7 +117,7 @@ def dist_info():
 class Step:
     """Inputs, outputs and launch order of one forward's fused-op sequence."""
 
-    def __init__(self, shape: W.Shape, fp8: bool, device, seed: int):
+    def __init__(self, shape: W.Shape, fp8: bool, device, seed: int, distinct: bool = True):
         import anima_flat_b200 as afb
 
         self.afb = afb
@@ -141,15 +142,21 @@ class Step:
         self.kw = [1.0 + 0.02 * torch.randn(hd, generator=g, device=device) for _ in range(L)]
         self.xw = [1.0 + 0.02 * torch.randn(hd, generator=g, device=device) for _ in range(L)]
         # Distinct inputs per call: the residual stream too, so that no call reads
-        # data a previous call left in L2.
+        # data a previous call left in L2.  With distinct=False (workloads whose
+        # tensors are each far larger than L2) two input sets alternate.
+        nset = L if distinct else 2
         self.z0 = act(B, S, D)
-        self.qkv = [act(B, S, 3 * H * hd) for _ in range(L)]
-        self.sub = [[act(B, S, D) for _ in range(3)] for _ in range(L)]   # o1, o2, mlp out
-        self.res = [[act(B, S, D) for _ in range(3)] for _ in range(L)]
-        self.xq = [act(B, S, D) for _ in range(L)]
+        self.qkv = [act(B, S, 3 * H * hd) for _ in range(nset)]
+        self.sub = [[act(B, S, D) for _ in range(3)] for _ in range(nset)]   # o1, o2, mlp out
+        self.res = [[act(B, S, D) for _ in range(3)] for _ in range(nset)]
+        self.xq = [act(B, S, D) for _ in range(nset)]
         if fp8:
-            self.attn = [[act(B, S, D) for _ in range(2)] for _ in range(L)]
-            self.up = [act(B, S, s.mlp) for _ in range(L)]
+            self.attn = [[act(B, S, D) for _ in range(2)] for _ in range(nset)]
+            self.up = [act(B, S, s.mlp) for _ in range(nset)]
+        if not distinct:
+            for name in ("qkv", "sub", "res", "xq") + (("attn", "up") if fp8 else ()):
+                lst = getattr(self, name)
+                setattr(self, name, [lst[i % 2] for i in range(L)])
         self.timed = "residual_adaln_fp8" if fp8 else "residual_adaln"
         self.timed_hook = None  # called around launches of self.timed when instrumenting
         self.only = None  # run only the launches of this op (roofline timing)
@@ -281,8 +288,14 @@ def run_ours(args, world, rank, local):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     _lib.set_pdl(not args.no_pdl)
-    shape = W.Shape(batch=2 if args.workload == "cfg3" else 1)
-    step = Step(shape, fp8=args.workload == "cfg3", device=device, seed=1234 + rank)
+    if args.workload == "cfg5":
+        # config 5: 32 sequences (batch 16 with CFG) sharded over the ranks
+        seqs = shard_sequences(32, world, rank)
+        shape = W.Shape(batch=len(seqs))
+        step = Step(shape, fp8=False, device=device, seed=1234 + rank, distinct=False)
+    else:
+        shape = W.Shape(batch=2 if args.workload == "cfg3" else 1)
+        step = Step(shape, fp8=args.workload == "cfg3", device=device, seed=1234 + rank)
     n_launch = len(step.calls)
 
     g = capture(step)
@@ -310,14 +323,15 @@ def run_ours(args, world, rank, local):
     ms_local = t0.elapsed_time(t1)
     clocks = sampler.stop()
 
-    ms = ms_local
-    if world > 1:
-        t = torch.tensor([ms_local], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    total_bytes = step.bytes * world * args.steps
+    ms = max_over_ranks(ms_local, device)
+    scaling = "strong" if args.workload == "cfg5" else "weak"
+    if scaling == "strong":
+        total_bytes = W.step_bytes(step.calls, W.Shape(batch=32)) * args.steps
+        rows_total = 32 * shape.seq * args.steps
+    else:
+        total_bytes = step.bytes * world * args.steps
+        rows_total = shape.rows * world * args.steps
     value = total_bytes / (ms * 1e-3) / 1e9
-    rows_total = shape.rows * world * args.steps
     del g
 
     # --- dominant kernel: the step's launches of it alone, back to back ---
@@ -363,16 +377,19 @@ def run_ours(args, world, rank, local):
         "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling,
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.1) modulation; no dataset needed)",
         "config": {
-            "workload": ("cfg2: Cosmos-Predict2-2B BF16 forward fused-op sequence (forward_fused), "
-                         "1024x1024, 28 blocks, 141 launches")
-            if not step.fp8 else
-            ("cfg3: Cosmos-Predict2-2B FP8 forward fused-op sequence (forward_fp8) with CFG batch 2, "
-             f"{n_launch} launches"),
+            "workload": {
+                "cfg2": "cfg2: Cosmos-Predict2-2B BF16 forward fused-op sequence (forward_fused), "
+                        "1024x1024, 28 blocks, 141 launches",
+                "cfg3": "cfg3: Cosmos-Predict2-2B FP8 forward fused-op sequence (forward_fp8) with "
+                        f"CFG batch 2, {n_launch} launches",
+                "cfg5": "cfg5: the cfg2 op sequence over 32 sequences x 4096 tokens (batch 16 with "
+                        "CFG), sequences sharded over the GPUs",
+            }[args.workload],
             "global_batch": shape.batch * world,
             "seq_len": shape.seq,
             "rows_per_gpu": shape.rows,
@@ -481,11 +498,7 @@ def run_e2e(step: Step, shape: W.Shape, args, world, device, barrier) -> dict:
     b.record()
     torch.cuda.synchronize()
     barrier()
-    ms = a.elapsed_time(b)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(a.elapsed_time(b), device)
     calls = W.bf16_forward_calls(s)
     val = W.step_bytes(calls, s) * world * n / (ms * 1e-3) / 1e9
     return {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
@@ -695,7 +708,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5"], default="cfg2")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
