@@ -33,6 +33,8 @@ SIGNATURES: dict[str, tuple] = {
     "afb_residual_adaln_bwd": (_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _P,
                                ctypes.c_size_t, _P),
     "afb_adaln_bwd": (_P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _P, ctypes.c_size_t, _P),
+    "afb_residual_adaln_bwd_noalloc": (_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I,
+                                       _F, _P),
     "afb_qkv_norm_rope_bwd": (_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P,
                               ctypes.c_size_t, _P),
     "afb_head_norm_bwd": (_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, ctypes.c_size_t, _P),

@@ -17,6 +17,9 @@
 // sums combine as a stride tree, (p0 + p2) + (p1 + p3); the finalize kernel adds the chunk
 // sums in increasing chunk order and rounds to bf16.  The chunk sums live in
 // a caller-provided fp32 workspace [B][chunks][NQ][D].
+#include <map>
+#include <mutex>
+
 #include "afb_device.cuh"
 #include "afb_launch.h"
 
@@ -285,9 +288,79 @@ int adaln_bwd_impl(const char* name, const void* gh, const void* gz, const void*
   return g.done(e);
 }
 
+// ---------------------------------------------------------------------------
+// Scratch for afb_residual_adaln_bwd_noalloc: some callers of this library
+// cannot allocate device memory at all (a host binding with no device
+// allocator of its own, or a serving process whose device memory is fully
+// reserved at start-up and which forbids allocation on the hot path).  For
+// them the parameter-gradient partials live in this file-scope array
+// instead of a caller-provided workspace.  Every GPU that loads the library
+// holds these 16 MiB until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of the scratch array for the current device.  The name of
+// the array is only a host-side stand-in; the address is looked up once per
+// device (with that device current) and cached.
+static cudaError_t noalloc_scratch(void** ptr) {
+  static std::mutex mu;
+  static std::map<int, void*> cache;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) {
+    *ptr = it->second;
+    return cudaSuccess;
+  }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  cache.emplace(dev, p);
+  *ptr = p;
+  return cudaSuccess;
+}
+
 }  // namespace afb
 
 using namespace afb;
+
+// Allocation-free variant of afb_residual_adaln_bwd (see the scratch comment
+// above).  The first call on a device looks up the scratch address; make that
+// first call before any stream capture.  The partial sums it keeps there are
+// fully overwritten by every call, so nothing needs clearing, but all calls
+// share the one array: calls that overlap on the GPU (other streams, other
+// threads) race.  Sizes whose partials exceed 16 MiB are rejected.
+extern "C" int afb_residual_adaln_bwd_noalloc(const void* gh, const void* gz, const void* z,
+                                              const void* x, const void* gate, const void* scale,
+                                              void* dx, void* dres, void* dgate, void* dshift,
+                                              void* dscale, int64_t batch, int64_t seq,
+                                              int64_t dim, float eps, void* stream) {
+  const char* name = "afb_residual_adaln_bwd_noalloc";
+  if (batch >= 0 && seq >= 1 && dim >= 1 &&
+      adaln_bwd_workspace(batch, seq, dim, true) > kNoAllocScratchBytes) {
+    set_error(std::string(name) + ": this size needs " +
+              std::to_string(adaln_bwd_workspace(batch, seq, dim, true)) +
+              " bytes of scratch, more than the " + std::to_string(kNoAllocScratchBytes) +
+              " bytes this entry point holds; use afb_residual_adaln_bwd with a workspace");
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  if (x == nullptr) {
+    set_error(std::string(name) + ": x is null");
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  void* scratch = nullptr;
+  const cudaError_t e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) {
+    set_error(std::string(name) + ": cannot resolve the scratch array: " + cudaGetErrorString(e));
+    return static_cast<int>(e);
+  }
+  return adaln_bwd_impl(name, gh, gz, z, x, gate, scale, dres, dx, dgate, dshift, dscale, batch,
+                        seq, dim, eps, scratch, kNoAllocScratchBytes,
+                        static_cast<cudaStream_t>(stream));
+}
 
 extern "C" size_t afb_residual_adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim) {
   return adaln_bwd_workspace(batch, seq, dim, true);

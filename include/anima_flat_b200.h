@@ -138,6 +138,22 @@ int afb_residual_adaln_bwd(const void* gh, const void* gz, const void* z, const 
                            int64_t seq, int64_t dim, float eps, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of afb_residual_adaln_bwd, for callers that cannot
+ * allocate device memory (a binding with no device allocator, or a process
+ * that reserves all device memory up front and forbids allocation on the
+ * hot path).  It has no counterpart in the reference.  Same arguments and
+ * outputs, without the workspace: the partial sums live in a 16 MiB array
+ * inside the library, which every GPU that loads the library holds until
+ * exit.  Sizes needing more (batch * ceil(seq/16) * 3 * dim * 4 bytes) are
+ * rejected.  The first call on a device resolves the array's address; make
+ * it before any stream capture.  All calls share the array: calls that
+ * overlap on the GPU race. */
+int afb_residual_adaln_bwd_noalloc(const void* gh, const void* gz, const void* z,
+                                   const void* x, const void* gate, const void* scale,
+                                   void* dx, void* dres, void* dgate, void* dshift,
+                                   void* dscale, int64_t batch, int64_t seq, int64_t dim,
+                                   float eps, void* stream);
+
 /* Replaces src/kernels/adaln.py:247-252 (anima_flat::adaln_bwd, HAS_X=False,
  * HAS_GZ=False): dz, dshift, dscale. */
 size_t afb_adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim);
