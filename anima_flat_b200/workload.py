@@ -63,6 +63,28 @@ def bytes_rowquant(s: Shape, K: int) -> int:
     return s.rows * (K * 2 + K + 4)
 
 
+def bytes_residual_adaln_bwd(s: Shape) -> int:
+    # read gh, gz, z, x; write dres, dx; gate/scale in, dgate/dshift/dscale out
+    return s.rows * s.dim * 2 * 6 + 5 * s.batch * s.dim * 2
+
+
+def bytes_adaln_bwd(s: Shape) -> int:
+    # read gh, z; write dz; scale in, dshift/dscale out
+    return s.rows * s.dim * 2 * 3 + 3 * s.batch * s.dim * 2
+
+
+def bytes_qkv_norm_rope_bwd(s: Shape) -> int:
+    w = s.heads * s.head_dim
+    # read the q/k sections of qkv and dq, dk, dv; write dqkv (all three sections)
+    tables = 2 * s.seq * (s.head_dim // 2) * 4
+    return s.rows * (2 * w + 3 * w + 3 * w) * 2 + tables + 4 * s.head_dim * 4
+
+
+def bytes_head_norm_bwd(s: Shape) -> int:
+    w = s.heads * s.head_dim
+    return s.rows * 3 * w * 2 + 2 * s.head_dim * 4
+
+
 def bf16_forward_calls(s: Shape) -> list[str]:
     """Op names in call order for forward_fused (model.py:366-375)."""
     calls = ["adaln"]
@@ -96,6 +118,10 @@ def call_bytes(name: str, s: Shape) -> int:
         "residual_adaln_fp8": bytes_residual_adaln_fp8,
         "rowquant": lambda sh: bytes_rowquant(sh, sh.dim),
         "rowquant_gelu": lambda sh: bytes_rowquant(sh, sh.mlp),
+        "residual_adaln_bwd": bytes_residual_adaln_bwd,
+        "adaln_bwd": bytes_adaln_bwd,
+        "qkv_norm_rope_bwd": bytes_qkv_norm_rope_bwd,
+        "head_norm_bwd": bytes_head_norm_bwd,
     }[name](s)
 
 

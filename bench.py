@@ -608,7 +608,8 @@ def run_reference(args, world, rank):
 
 # ------------------------------------------------------------- per-op table --
 PER_OPS = ["residual_adaln", "adaln", "qkv_norm_rope", "head_norm", "residual_adaln_fp8",
-           "adaln_fp8", "rowquant", "rowquant_gelu"]
+           "adaln_fp8", "rowquant", "rowquant_gelu", "residual_adaln_bwd", "adaln_bwd",
+           "qkv_norm_rope_bwd", "head_norm_bwd"]
 
 
 def run_per_op(args):
@@ -648,6 +649,24 @@ def run_per_op(args):
         elif name == "head_norm":
             sets = [(act(B, S, H * hd), w, H) for _ in range(nbuf)]
             fn = afb.head_norm
+        elif name == "residual_adaln_bwd":   # config 4 shapes (B=1), grads N(0, 1e-2)
+            ops = torch.ops.anima_flat_b200
+            sets = [(act(B, S, D) * 0.01, act(B, S, D) * 0.01, act(B, S, D), act(B, S, D), vec(),
+                     vec() + 1, 1e-6) for _ in range(nbuf)]
+            fn = ops.residual_adaln_bwd
+        elif name == "adaln_bwd":
+            ops = torch.ops.anima_flat_b200
+            sets = [(act(B, S, D) * 0.01, act(B, S, D), vec() + 1, 1e-6) for _ in range(nbuf)]
+            fn = ops.adaln_bwd
+        elif name == "qkv_norm_rope_bwd":
+            ops = torch.ops.anima_flat_b200
+            sets = [(act(B, S, 3 * H * hd), act(B, S, H, hd) * 0.01, act(B, S, H, hd) * 0.01,
+                     act(B, S, H, hd) * 0.01, w, w, cos, sin, H, 1e-5) for _ in range(nbuf)]
+            fn = ops.qkv_norm_rope_bwd
+        elif name == "head_norm_bwd":
+            ops = torch.ops.anima_flat_b200
+            sets = [(act(B, S, H * hd), act(B, S, H, hd) * 0.01, w, H, 1e-5) for _ in range(nbuf)]
+            fn = ops.head_norm_bwd
         else:
             K = s.mlp if name == "rowquant_gelu" else D
             sets = [(act(B, S, K),) for _ in range(nbuf)]
