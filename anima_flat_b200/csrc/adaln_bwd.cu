@@ -14,8 +14,8 @@
 // Parameter-gradient order (deterministic, independent of the launch shape):
 // the rows of each batch entry are cut into chunks of kChunkRows; in a chunk,
 // warp w sums rows w, w + 4, w + 8, ... in increasing order; the four warp
-// sums combine as a stride tree, (p0 + p2) + (p1 + p3); the finalize kernel adds the chunk
-// sums in increasing chunk order and rounds to bf16.  The chunk sums live in
+// sums combine as a stride tree, (p0 + p2) + (p1 + p3); the chunk sums combine
+// by a stride tree over the chunk index (finalize.cu) and round to bf16.  The chunk sums live in
 // a caller-provided fp32 workspace [B][chunks][NQ][D].
 #include <map>
 #include <mutex>
@@ -63,19 +63,20 @@ adaln_bwd_kernel(const AdalnBwdArgs a) {
   const int64_t b = blockIdx.y;
   const int64_t chunk = blockIdx.x;
   const int64_t pbase = b * D;
-  float* acc = acc_all + static_cast<int64_t>(warp) * NQ * D;
+  // Per-warp accumulators, NQ planes of NC*256 floats laid out [c][half][lane][4]
+  // so that every warp-wide float4 access is 512 contiguous bytes.
+  constexpr int kPlane = NC * 256;
+  float* acc = acc_all + static_cast<int64_t>(warp) * NQ * kPlane;
+  auto slot = [&](int q, int c, int half) {
+    return reinterpret_cast<float4*>(acc + q * kPlane + ((c * 2 + half) * 32 + lane) * 4);
+  };
   const float fd = static_cast<float>(D);
-
-  // zero this warp's accumulators (lane owns its own columns)
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
-    const int e = (lane + 32 * c) * 8;
-    if (e < D) {
 #pragma unroll
-      for (int q = 0; q < NQ; ++q) {
-        reinterpret_cast<float4*>(acc + q * D + e)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-        reinterpret_cast<float4*>(acc + q * D + e)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+    for (int q = 0; q < NQ; ++q) {
+      *slot(q, c, 0) = make_float4(0.f, 0.f, 0.f, 0.f);
+      *slot(q, c, 1) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
 
@@ -133,19 +134,16 @@ adaln_bwd_kernel(const AdalnBwdArgs a) {
         unpack8(ld_keep(a.gate + pbase + e), g8);
         unpack8(ld_stream(a.x + base + e), x8);
       }
-      float4* a_sh = reinterpret_cast<float4*>(acc + e);
-      float4* a_sc = reinterpret_cast<float4*>(acc + D + e);
       float sh_acc[8], sc_acc[8], g_acc[8];
       {
-        const float4 p0 = a_sh[0], p1 = a_sh[1], q0 = a_sc[0], q1 = a_sc[1];
+        const float4 p0 = *slot(0, c, 0), p1 = *slot(0, c, 1), q0 = *slot(1, c, 0), q1 = *slot(1, c, 1);
         sh_acc[0] = p0.x; sh_acc[1] = p0.y; sh_acc[2] = p0.z; sh_acc[3] = p0.w;
         sh_acc[4] = p1.x; sh_acc[5] = p1.y; sh_acc[6] = p1.z; sh_acc[7] = p1.w;
         sc_acc[0] = q0.x; sc_acc[1] = q0.y; sc_acc[2] = q0.z; sc_acc[3] = q0.w;
         sc_acc[4] = q1.x; sc_acc[5] = q1.y; sc_acc[6] = q1.z; sc_acc[7] = q1.w;
       }
       if (HAS_X) {
-        const float4* a_g = reinterpret_cast<const float4*>(acc + 2 * D + e);
-        const float4 r0 = a_g[0], r1 = a_g[1];
+        const float4 r0 = *slot(2, c, 0), r1 = *slot(2, c, 1);
         g_acc[0] = r0.x; g_acc[1] = r0.y; g_acc[2] = r0.z; g_acc[3] = r0.w;
         g_acc[4] = r1.x; g_acc[5] = r1.y; g_acc[6] = r1.z; g_acc[7] = r1.w;
       }
@@ -167,14 +165,13 @@ adaln_bwd_kernel(const AdalnBwdArgs a) {
       }
       st16(a.dz + base + e, pack8_rn(dzf));
       if (HAS_X) st16(a.dx + base + e, pack8_rn(dxf));
-      a_sh[0] = make_float4(sh_acc[0], sh_acc[1], sh_acc[2], sh_acc[3]);
-      a_sh[1] = make_float4(sh_acc[4], sh_acc[5], sh_acc[6], sh_acc[7]);
-      a_sc[0] = make_float4(sc_acc[0], sc_acc[1], sc_acc[2], sc_acc[3]);
-      a_sc[1] = make_float4(sc_acc[4], sc_acc[5], sc_acc[6], sc_acc[7]);
+      *slot(0, c, 0) = make_float4(sh_acc[0], sh_acc[1], sh_acc[2], sh_acc[3]);
+      *slot(0, c, 1) = make_float4(sh_acc[4], sh_acc[5], sh_acc[6], sh_acc[7]);
+      *slot(1, c, 0) = make_float4(sc_acc[0], sc_acc[1], sc_acc[2], sc_acc[3]);
+      *slot(1, c, 1) = make_float4(sc_acc[4], sc_acc[5], sc_acc[6], sc_acc[7]);
       if (HAS_X) {
-        float4* a_g = reinterpret_cast<float4*>(acc + 2 * D + e);
-        a_g[0] = make_float4(g_acc[0], g_acc[1], g_acc[2], g_acc[3]);
-        a_g[1] = make_float4(g_acc[4], g_acc[5], g_acc[6], g_acc[7]);
+        *slot(2, c, 0) = make_float4(g_acc[0], g_acc[1], g_acc[2], g_acc[3]);
+        *slot(2, c, 1) = make_float4(g_acc[4], g_acc[5], g_acc[6], g_acc[7]);
       }
     }
   }
@@ -182,41 +179,22 @@ adaln_bwd_kernel(const AdalnBwdArgs a) {
   // Chunk partial: stride tree over the warps, (p0 + p2) + (p1 + p3).
   __syncthreads();
   float* out = a.part + ((b * a.chunks + chunk) * NQ) * D;
-  const int n = NQ * D;
-  const int64_t stride = static_cast<int64_t>(NQ) * D;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  const int stride = NQ * kPlane;
+  for (int i = threadIdx.x; i < NQ * kPlane; i += blockDim.x) {
+    const int q = i / kPlane, r = i % kPlane;
+    const int kk = r & 3, ln = (r >> 2) & 31, half = (r >> 7) & 1, c = r >> 8;
+    const int col = (ln + 32 * c) * 8 + half * 4 + kk;
+    if (col >= D) continue;
     const float p0 = acc_all[i], p1 = acc_all[stride + i];
     const float p2 = acc_all[2 * stride + i], p3 = acc_all[3 * stride + i];
-    out[i] = __fadd_rn(__fadd_rn(p0, p2), __fadd_rn(p1, p3));
+    out[q * D + col] = __fadd_rn(__fadd_rn(p0, p2), __fadd_rn(p1, p3));
   }
-}
-
-// dparam[b, q, col] = bf16(sum over chunks, in increasing order).
-__global__ void adaln_bwd_finalize_kernel(const float* part, uint16_t* dshift, uint16_t* dscale,
-                                          uint16_t* dgate, int64_t chunks, int nq, int D) {
-  pdl_wait();
-  pdl_trigger();
-  const int64_t b = blockIdx.y;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= nq * D) return;
-  const float* p = part + b * chunks * nq * D + i;
-  float s = 0.0f;
-  int64_t c = 0;
-  for (; c + 4 <= chunks; c += 4) {
-    const float v0 = p[(c + 0) * nq * D], v1 = p[(c + 1) * nq * D];
-    const float v2 = p[(c + 2) * nq * D], v3 = p[(c + 3) * nq * D];
-    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v0), v1), v2), v3);
-  }
-  for (; c < chunks; ++c) s = __fadd_rn(s, p[c * nq * D]);
-  const int q = i / D, col = i % D;
-  uint16_t* dst = q == 0 ? dshift : q == 1 ? dscale : dgate;
-  dst[b * D + col] = static_cast<uint16_t>(pack2_rn(s, 0.0f) & 0xffffu);
 }
 
 template <bool HAS_X, bool HAS_GZ>
 static cudaError_t launch_adaln_bwd(const AdalnBwdArgs& a, int64_t batch, cudaStream_t st) {
   constexpr int NQ = bwd_nq<HAS_X>();
-  const size_t smem = static_cast<size_t>(kBwdWarps) * NQ * a.dim * sizeof(float);
+  const size_t smem = static_cast<size_t>(kBwdWarps) * NQ * row_chunks(a.dim) * 256 * sizeof(float);
   const dim3 grid(static_cast<unsigned>(a.chunks), static_cast<unsigned>(batch));
   const dim3 block(kBwdWarps * 32);
   cudaError_t e = cudaErrorInvalidValue;
@@ -252,6 +230,8 @@ int adaln_bwd_impl(const char* name, const void* gh, const void* gz, const void*
   const bool has_x = x != nullptr;
   if (!check_rows(batch, seq, dim) ||
       !check(dim <= 2048, "backward supports dim <= 2048, got " + std::to_string(dim)) ||
+      !check(finalize_fits((seq + kChunkRows - 1) / kChunkRows),
+             "backward supports seq <= " + std::to_string(32768 * kChunkRows)) ||
       !check_ptrs({gh, z, scale, dz, dshift, dscale}, {"gh", "z", "scale", "dz", "dshift", "dscale"}) ||
       (gz != nullptr && !check_ptrs({gz}, {"gz"})) ||
       (has_x && !check_ptrs({gate, dx, dgate}, {"gate", "dx", "dgate"})) ||
@@ -279,13 +259,16 @@ int adaln_bwd_impl(const char* name, const void* gh, const void* gz, const void*
   if (has_x) e = gz ? launch_adaln_bwd<true, true>(a, batch, st) : launch_adaln_bwd<true, false>(a, batch, st);
   else e = gz ? launch_adaln_bwd<false, true>(a, batch, st) : launch_adaln_bwd<false, false>(a, batch, st);
   if (e != cudaSuccess) return g.done(e);
-  const int nq = has_x ? 3 : 2;
-  const dim3 fgrid(static_cast<unsigned>((nq * dim + 255) / 256), static_cast<unsigned>(batch));
-  e = launch_pdl(adaln_bwd_finalize_kernel, fgrid, dim3(256), 0, st,
-                 static_cast<const float*>(workspace), static_cast<uint16_t*>(dshift),
-                 static_cast<uint16_t*>(dscale), static_cast<uint16_t*>(dgate), a.chunks, nq,
-                 static_cast<int>(dim));
-  return g.done(e);
+  FinalizeArgs f{};
+  f.part = static_cast<const float*>(workspace);
+  f.n = a.chunks;
+  f.ncols = (has_x ? 3 : 2) * static_cast<int>(dim);
+  f.seg = static_cast<int>(dim);
+  f.out[0] = dshift;
+  f.out[1] = dscale;
+  f.out[2] = dgate;
+  f.bf16_out = 1;
+  return g.done(launch_colsum_finalize(f, batch, st));
 }
 
 // ---------------------------------------------------------------------------

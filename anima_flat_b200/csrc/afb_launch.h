@@ -38,6 +38,22 @@ bool pdl_enabled();
 // Host readers of the per-file device status words (OR-ed by afb_device_status).
 cudaError_t read_status_adaln_fwd(int* status);
 cudaError_t read_status_headnorm_fwd(int* status);
+cudaError_t read_status_headnorm_bwd(int* status);
+
+// Column sums of chunk partials part[batch][n][ncols] (fp32) by a stride tree
+// over the chunk index (finalize.cu); column c goes to out[c / seg][b*seg +
+// c % seg], rounded to bf16 (RNE) or kept fp32.
+struct FinalizeArgs {
+  const float* part;
+  int64_t n;
+  int ncols;
+  int seg;
+  void* out[3];
+  int bf16_out;
+  int np;  // set by the launcher
+};
+bool finalize_fits(int64_t n);
+cudaError_t launch_colsum_finalize(const FinalizeArgs& f, int64_t batch, cudaStream_t st);
 
 // Records `msg` as this thread's last error (read by afb_last_error()).
 void set_error(const std::string& msg);

@@ -11,21 +11,27 @@
 //   dw += d' * xhat   (fp32, per dim)
 // v's gradient is copied into the v third of dqkv (rope.py:304-326).
 //
-// Layout as the forward: one warp per token, LPH = hd/8 lanes per head.
+// Layout: persistent CTAs of kHnbWarps warps walk fixed chunks of kHnbWarps
+// tokens; warp w takes token w of each chunk.  Lane 0 streams the token's
+// forward input (the contiguous q|k span, or x) and upstream gradients into a
+// shared-memory stage with bulk copies completing on an mbarrier.  A head
+// spans L = hd/16 lanes; lane l holds dims [8l, 8l+8) of both halves, so the
+// rotation pairs are in the lane and the per-head sums follow the forward's
+// canonical order.
+//
 // Weight-gradient order (deterministic, independent of the launch shape):
-// tokens are cut into chunks of kTokChunk; in a chunk, warp w takes tokens
-// w, w + 4, ...; lane group g (lanes g*LPH .. g*LPH+LPH-1) takes heads
-// g, g + 32/LPH, ...; each (chunk, warp, group) slot sums its (token, head)
-// terms in that order starting from zero, and the finalize kernel adds the
-// slots in increasing slot order.
+// per token, lane group g sums heads g, g + 32/L, ... in increasing order and
+// the groups combine as a stride tree; the kHnbWarps token sums of a chunk
+// combine as a stride tree over the token index; the chunk sums combine as a
+// stride tree over the chunk index (finalize.cu).
 #include "afb_device.cuh"
 #include "afb_launch.h"
 
 namespace afb {
 
-constexpr int kHnWarps = 4;
-constexpr int kTokPerWarp = 4;
-constexpr int kTokChunk = kHnWarps * kTokPerWarp;
+constexpr int kHnbWarps = 8;       // warps per CTA = tokens per chunk
+constexpr int kHnbMaxStages = 4;
+constexpr int kHnbUnroll = 2;
 
 struct HeadNormBwdArgs {
   const uint16_t* src;  // forward input rows (qkv or x)
@@ -39,7 +45,7 @@ struct HeadNormBwdArgs {
   const float* cos;
   const float* sin;
   uint16_t* dsrc;       // [tokens, src_row]
-  float* part;          // [slots][NSEC][hd], slots = chunks * kHnWarps * (32 / LPH)
+  float* part;          // [chunks][NSEC][hd] chunk sums of the weight gradient
   int64_t tokens;
   int64_t seq;
   int heads;
@@ -47,174 +53,297 @@ struct HeadNormBwdArgs {
 };
 
 template <int HD, bool ROTATE, bool WITH_K, bool WITH_V>
-__global__ void __launch_bounds__(kHnWarps * 32)
-headnorm_bwd_kernel(const HeadNormBwdArgs a) {
-  constexpr int LPH = HD / 8;
-  constexpr int HPI = 32 / LPH;
+__global__ void __launch_bounds__(kHnbWarps * 32, 1)
+headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
+  constexpr int L = HD / 16;
+  constexpr int HPI = 32 / L;
   constexpr int HALF = HD / 2;
   constexpr int NSEC = WITH_K ? 2 : 1;
-  pdl_wait();
-  pdl_trigger();
+  extern __shared__ __align__(128) uint8_t smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int j = lane % LPH;
-  const int grp = lane / LPH;
+  const int l = lane % L;
+  const int grp = lane / L;
   const int H = a.heads;
   const int iters = (H + HPI - 1) / HPI;
-  const int64_t chunk = blockIdx.x;
-  const float fhd = static_cast<float>(HD);
-
-  float wacc[NSEC][8];
-  float w[NSEC][8];
-#pragma unroll
-  for (int sec = 0; sec < NSEC; ++sec) {
-    const float* wp = (sec ? a.wk : a.wq) + 8 * j;
-    const float4 w0 = ld_keep_f4(wp), w1 = ld_keep_f4(wp + 4);
-    w[sec][0] = w0.x; w[sec][1] = w0.y; w[sec][2] = w0.z; w[sec][3] = w0.w;
-    w[sec][4] = w1.x; w[sec][5] = w1.y; w[sec][6] = w1.z; w[sec][7] = w1.w;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) wacc[sec][k] = 0.0f;
+  const uint32_t sec_bytes = static_cast<uint32_t>(H) * HD * 2u;
+  // stage: forward input sections (contiguous), then one upstream gradient per section
+  const uint32_t stage_bytes = 2u * NSEC * sec_bytes;
+  float* xch = reinterpret_cast<float*>(smem);  // [warps][NSEC][HD] token sums
+  uint8_t* ring = smem + kHnbWarps * NSEC * HD * sizeof(float) +
+                  static_cast<size_t>(warp) * nsw * stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kHnbWarps * NSEC * HD * sizeof(float) +
+                                               static_cast<size_t>(kHnbWarps) * nsw * stage_bytes) +
+                   warp * nsw;
+  if (lane == 0) {
+    for (int s = 0; s < nsw; ++s) mbar_init(smem_addr(&bars[s]), 1);
+    fence_mbar_init();
   }
-
-  for (int i = 0; i < kTokPerWarp; ++i) {
-    const int64_t tok = chunk * kTokChunk + i * kHnWarps + warp;
-    if (tok >= a.tokens) break;  // warp-uniform
-    float cs[8], sn[8];
-    if (ROTATE) {
-      const int64_t pos = tok % a.seq;
-      const float* cp = a.cos + pos * HALF + (8 * j) % HALF;
-      const float* sp = a.sin + pos * HALF + (8 * j) % HALF;
-      const float4 c0 = ld_keep_f4(cp), c1 = ld_keep_f4(cp + 4);
-      const float4 s0 = ld_keep_f4(sp), s1 = ld_keep_f4(sp + 4);
-      cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
-      cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
-      sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-    }
-    const uint16_t* row = a.src + tok * a.src_row;
-    uint16_t* drow = a.dsrc + tok * a.src_row;
-    const int64_t gbase = tok * static_cast<int64_t>(H) * HD;
-#pragma unroll
-    for (int sec = 0; sec < NSEC; ++sec) {
-      const uint16_t* in = row + (sec ? a.k_off : a.q_off);
-      const uint16_t* dout = (sec ? a.dk : a.dq) + gbase;
-      uint16_t* dst = drow + (sec ? a.k_off : a.q_off);
-      for (int it = 0; it < iters; ++it) {
-        const int h = it * HPI + grp;
-        const bool hv = h < H;
-        const uint4 xv = hv ? ld_stream(in + h * HD + 8 * j) : make_uint4(0, 0, 0, 0);
-        const uint4 gv = hv ? ld_stream(dout + h * HD + 8 * j) : make_uint4(0, 0, 0, 0);
-        float x[8], d[8];
-        unpack8(xv, x);
-        unpack8(gv, d);
-        if (ROTATE) {
-          uint4 pg;
-          pg.x = __shfl_xor_sync(kFull, gv.x, LPH / 2);
-          pg.y = __shfl_xor_sync(kFull, gv.y, LPH / 2);
-          pg.z = __shfl_xor_sync(kFull, gv.z, LPH / 2);
-          pg.w = __shfl_xor_sync(kFull, gv.w, LPH / 2);
-          float p[8];
-          unpack8(pg, p);
-          const bool first = j < LPH / 2;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float mc = __fmul_rn(d[k], cs[k]);
-            const float ps = __fmul_rn(p[k], sn[k]);
-            d[k] = first ? __fadd_rn(mc, ps) : __fsub_rn(mc, ps);
-          }
-        }
-        float t[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) t[k] = __fmul_rn(x[k], x[k]);
-        const float rstd = canonical_rstd(__fdiv_rn(group_canonical_sum<LPH>(t), fhd), a.eps);
-        float xh[8], u[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          xh[k] = __fmul_rn(x[k], rstd);
-          u[k] = __fmul_rn(d[k], w[sec][k]);
-          t[k] = __fmul_rn(u[k], xh[k]);
-        }
-        const float c = __fdiv_rn(group_canonical_sum<LPH>(t), fhd);
-        float o[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          o[k] = __fmul_rn(rstd, __fsub_rn(u[k], __fmul_rn(xh[k], c)));
-          if (hv) wacc[sec][k] = __fadd_rn(wacc[sec][k], __fmul_rn(d[k], xh[k]));
-        }
-        if (hv) st16(dst + h * HD + 8 * j, pack8_rn(o));
-      }
-    }
-    if (WITH_V) {
-      const uint16_t* in = a.dv + gbase;
-      uint16_t* out = drow + a.v_off;
-      const int nvec = H * HD / 8;
-      for (int v = lane; v < nvec; v += 32) st16(out + 8 * v, ld_stream(in + 8 * v));
-    }
-  }
-
-  const int64_t slot = (chunk * kHnWarps + warp) * HPI + grp;
-#pragma unroll
-  for (int sec = 0; sec < NSEC; ++sec) {
-    float* out = a.part + (slot * NSEC + sec) * HD + 8 * j;
-    reinterpret_cast<float4*>(out)[0] = make_float4(wacc[sec][0], wacc[sec][1], wacc[sec][2], wacc[sec][3]);
-    reinterpret_cast<float4*>(out)[1] = make_float4(wacc[sec][4], wacc[sec][5], wacc[sec][6], wacc[sec][7]);
-  }
-}
-
-// dw[sec][dim] = sum over slots in increasing order.
-__global__ void headnorm_bwd_finalize_kernel(const float* part, float* dw0, float* dw1,
-                                             int64_t slots, int nsec, int hd) {
+  __syncwarp();
   pdl_wait();
   pdl_trigger();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= nsec * hd) return;
-  const float* p = part + i;
-  const int64_t stride = static_cast<int64_t>(nsec) * hd;
-  float s = 0.0f;
-  int64_t k = 0;
-  for (; k + 4 <= slots; k += 4) {
-    const float v0 = p[(k + 0) * stride], v1 = p[(k + 1) * stride];
-    const float v2 = p[(k + 2) * stride], v3 = p[(k + 3) * stride];
-    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v0), v1), v2), v3);
+
+  const int64_t chunks = (a.tokens + kHnbWarps - 1) / kHnbWarps;
+  // this warp's j-th token: token `warp` of chunk blockIdx.x + j*gridDim.x
+  auto token_of = [&](int64_t j) {
+    return (static_cast<int64_t>(blockIdx.x) + j * gridDim.x) * kHnbWarps + warp;
+  };
+  auto chunk_of = [&](int64_t j) { return static_cast<int64_t>(blockIdx.x) + j * gridDim.x; };
+  auto issue = [&](int64_t j) {  // lane 0
+    const int64_t tok = token_of(j);
+    const int s = static_cast<int>(j % nsw);
+    uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
+    const uint32_t bar = smem_addr(&bars[s]);
+    mbar_arrive_expect_tx(bar, stage_bytes);
+    bulk_g2s(smem_addr(st), a.src + tok * a.src_row + a.q_off, NSEC * sec_bytes, bar);
+    bulk_g2s(smem_addr(st + NSEC * sec_bytes), a.dq + tok * static_cast<int64_t>(H) * HD, sec_bytes, bar);
+    if (WITH_K)
+      bulk_g2s(smem_addr(st + 3 * sec_bytes), a.dk + tok * static_cast<int64_t>(H) * HD, sec_bytes, bar);
+  };
+  if (lane == 0) {
+    for (int j = 0; j < nsw && chunk_of(j) < chunks && token_of(j) < a.tokens; ++j) issue(j);
   }
-  for (; k < slots; ++k) s = __fadd_rn(s, p[k * stride]);
-  (i < hd ? dw0 : dw1)[i % hd] = s;
+
+  float w[NSEC][2][8];
+#pragma unroll
+  for (int sec = 0; sec < NSEC; ++sec) {
+    const float* wp = (sec ? a.wk : a.wq) + 8 * l;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const float4 w0 = ld_keep_f4(wp + hf * HALF), w1 = ld_keep_f4(wp + hf * HALF + 4);
+      w[sec][hf][0] = w0.x; w[sec][hf][1] = w0.y; w[sec][hf][2] = w0.z; w[sec][hf][3] = w0.w;
+      w[sec][hf][4] = w1.x; w[sec][hf][5] = w1.y; w[sec][hf][6] = w1.z; w[sec][hf][7] = w1.w;
+    }
+  }
+
+  bool dead = false;  // set if a bounded wait gave up: the warp then only joins the barriers
+  for (int64_t j = 0; chunk_of(j) < chunks; ++j) {
+    const int64_t tok = token_of(j);
+    const bool has = tok < a.tokens && !dead;
+    float wacc[NSEC][2][8];
+#pragma unroll
+    for (int sec = 0; sec < NSEC; ++sec)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) wacc[sec][hf][k] = 0.0f;
+    if (has) {
+      const int s = static_cast<int>(j % nsw);
+      const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
+      float cs[8], sn[8];
+      if (ROTATE) {
+        const int64_t pos = tok % a.seq;
+        const float* cp = a.cos + pos * HALF + 8 * l;
+        const float* sp = a.sin + pos * HALF + 8 * l;
+        const float4 c0 = ld_keep_f4(cp), c1 = ld_keep_f4(cp + 4);
+        const float4 s0 = ld_keep_f4(sp), s1 = ld_keep_f4(sp + 4);
+        cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+        cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+        sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+        sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+      }
+      if (WITH_V) {  // dqkv's v third is dv, unchanged
+        const uint16_t* in = a.dv + tok * static_cast<int64_t>(H) * HD;
+        uint16_t* out = a.dsrc + tok * a.src_row + a.v_off;
+        for (int v = lane; v < H * HD / 8; v += 32) st16(out + 8 * v, ld_stream(in + 8 * v));
+      }
+      if (!mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
+        for (int64_t k = j + 1; k < j + nsw && chunk_of(k) < chunks && token_of(k) < a.tokens; ++k)
+          mbar_wait(smem_addr(&bars[k % nsw]), static_cast<uint32_t>((k / nsw) & 1));
+        dead = true;
+      }
+#pragma unroll
+      for (int sec = 0; sec < NSEC && !dead; ++sec) {
+        const uint8_t* xin = st + sec * sec_bytes;
+        const uint8_t* gin = st + (NSEC + sec) * sec_bytes;
+        uint16_t* out = a.dsrc + tok * a.src_row + (sec ? a.k_off : a.q_off);
+        for (int it0 = 0; it0 < iters; it0 += kHnbUnroll) {
+          uint4 xa[kHnbUnroll], xb[kHnbUnroll];
+          float dpa[kHnbUnroll][8], dpb[kHnbUnroll][8];  // rotated-back gradient
+          float ss[kHnbUnroll];
+#pragma unroll
+          for (int u = 0; u < kHnbUnroll; ++u) {
+            const int h = (it0 + u) * HPI + grp;
+            const bool hv = it0 + u < iters && h < H;
+            const int o = (h * HD + 8 * l) * 2;
+            xa[u] = hv ? lds16(xin + o) : make_uint4(0, 0, 0, 0);
+            xb[u] = hv ? lds16(xin + o + HALF * 2) : make_uint4(0, 0, 0, 0);
+            const uint4 ga = hv ? lds16(gin + o) : make_uint4(0, 0, 0, 0);
+            const uint4 gb = hv ? lds16(gin + o + HALF * 2) : make_uint4(0, 0, 0, 0);
+            float fa[8], fb[8];
+            unpack8(ga, fa);
+            unpack8(gb, fb);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              if (ROTATE) {
+                dpa[u][k] = __fadd_rn(__fmul_rn(fa[k], cs[k]), __fmul_rn(fb[k], sn[k]));
+                dpb[u][k] = __fsub_rn(__fmul_rn(fb[k], cs[k]), __fmul_rn(fa[k], sn[k]));
+              } else {
+                dpa[u][k] = fa[k];
+                dpb[u][k] = fb[k];
+              }
+            }
+            unpack8(xa[u], fa);
+            unpack8(xb[u], fb);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              fa[k] = __fmul_rn(fa[k], fa[k]);
+              fb[k] = __fmul_rn(fb[k], fb[k]);
+            }
+            ss[u] = __fadd_rn(vec_sum8(fa), vec_sum8(fb));
+          }
+#pragma unroll
+          for (int o = L / 2; o >= 1; o >>= 1) {
+#pragma unroll
+            for (int u = 0; u < kHnbUnroll; ++u) ss[u] = __fadd_rn(ss[u], __shfl_xor_sync(kFull, ss[u], o));
+          }
+          float rstd[kHnbUnroll], cc[kHnbUnroll];
+#pragma unroll
+          for (int u = 0; u < kHnbUnroll; ++u) {
+            rstd[u] = canonical_rstd(__fmul_rn(ss[u], 1.0f / HD), a.eps);
+            float fa[8], fb[8], ta[8], tb[8];
+            unpack8(xa[u], fa);
+            unpack8(xb[u], fb);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              ta[k] = __fmul_rn(__fmul_rn(dpa[u][k], w[sec][0][k]), __fmul_rn(fa[k], rstd[u]));
+              tb[k] = __fmul_rn(__fmul_rn(dpb[u][k], w[sec][1][k]), __fmul_rn(fb[k], rstd[u]));
+            }
+            cc[u] = __fadd_rn(vec_sum8(ta), vec_sum8(tb));
+          }
+#pragma unroll
+          for (int o = L / 2; o >= 1; o >>= 1) {
+#pragma unroll
+            for (int u = 0; u < kHnbUnroll; ++u) cc[u] = __fadd_rn(cc[u], __shfl_xor_sync(kFull, cc[u], o));
+          }
+#pragma unroll
+          for (int u = 0; u < kHnbUnroll; ++u) {
+            const int h = (it0 + u) * HPI + grp;
+            if (it0 + u >= iters || h >= H) continue;
+            const float c = __fmul_rn(cc[u], 1.0f / HD);
+            float fa[8], fb[8], oa[8], ob[8];
+            unpack8(xa[u], fa);
+            unpack8(xb[u], fb);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float xha = __fmul_rn(fa[k], rstd[u]);
+              const float xhb = __fmul_rn(fb[k], rstd[u]);
+              const float ua = __fmul_rn(dpa[u][k], w[sec][0][k]);
+              const float ub = __fmul_rn(dpb[u][k], w[sec][1][k]);
+              oa[k] = __fmul_rn(rstd[u], __fsub_rn(ua, __fmul_rn(xha, c)));
+              ob[k] = __fmul_rn(rstd[u], __fsub_rn(ub, __fmul_rn(xhb, c)));
+              wacc[sec][0][k] = __fadd_rn(wacc[sec][0][k], __fmul_rn(dpa[u][k], xha));
+              wacc[sec][1][k] = __fadd_rn(wacc[sec][1][k], __fmul_rn(dpb[u][k], xhb));
+            }
+            st16(out + h * HD + 8 * l, pack8_rn(oa));
+            st16(out + h * HD + HALF + 8 * l, pack8_rn(ob));
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && !dead && chunk_of(j + nsw) < chunks && token_of(j + nsw) < a.tokens) {
+        fence_proxy_async_smem();
+        issue(j + nsw);
+      }
+    }
+    // token sum: stride tree over the lane groups (xor 16, then 8, ... down to L)
+#pragma unroll
+    for (int o = 16; o >= L; o >>= 1) {
+#pragma unroll
+      for (int sec = 0; sec < NSEC; ++sec)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            wacc[sec][hf][k] = __fadd_rn(wacc[sec][hf][k], __shfl_xor_sync(kFull, wacc[sec][hf][k], o));
+    }
+    if (grp == 0) {
+#pragma unroll
+      for (int sec = 0; sec < NSEC; ++sec)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) xch[(warp * NSEC + sec) * HD + hf * HALF + 8 * l + k] = wacc[sec][hf][k];
+    }
+    __syncthreads();
+    // chunk sum: stride tree over the warps (= tokens of the chunk)
+    for (int i = threadIdx.x; i < NSEC * HD; i += kHnbWarps * 32) {
+      float p[kHnbWarps];
+#pragma unroll
+      for (int t = 0; t < kHnbWarps; ++t) p[t] = xch[t * NSEC * HD + i];
+#pragma unroll
+      for (int hw = kHnbWarps / 2; hw >= 1; hw >>= 1)
+#pragma unroll
+        for (int t = 0; t < hw; ++t) p[t] = __fadd_rn(p[t], p[t + hw]);
+      a.part[chunk_of(j) * NSEC * HD + i] = p[0];
+    }
+    __syncthreads();
+  }
 }
 
-static int64_t hn_slots(int64_t tokens, int64_t hd) {
-  const int64_t chunks = (tokens + kTokChunk - 1) / kTokChunk;
-  return chunks * kHnWarps * (32 / (hd / 8));
-}
+static int64_t hn_chunks(int64_t tokens) { return (tokens + kHnbWarps - 1) / kHnbWarps; }
 
 size_t headnorm_bwd_workspace(int64_t tokens, int64_t hd, int nsec) {
-  return static_cast<size_t>(hn_slots(tokens, hd) * nsec * hd) * sizeof(float);
+  return static_cast<size_t>(hn_chunks(tokens) * nsec * hd) * sizeof(float);
 }
 
 template <bool ROTATE, bool WITH_K, bool WITH_V>
 static cudaError_t launch_headnorm_bwd(const HeadNormBwdArgs& a, int hd, cudaStream_t st) {
-  const dim3 grid(static_cast<unsigned>((a.tokens + kTokChunk - 1) / kTokChunk));
-  const dim3 block(kHnWarps * 32);
+  const DeviceInfo& dev = device_info();
+  if (dev.error != cudaSuccess) return dev.error;
+  constexpr int NSEC = WITH_K ? 2 : 1;
+  const size_t stage = 2 * NSEC * static_cast<size_t>(a.heads) * hd * 2;
+  const size_t fixed = static_cast<size_t>(kHnbWarps) * NSEC * hd * sizeof(float);
+  const size_t per = kHnbWarps * (stage + sizeof(uint64_t));
+  int nsw = static_cast<int>((dev.max_smem_optin - fixed) / per);
+  if (nsw < 1) return cudaErrorInvalidValue;  // bounded by heads * head_dim <= 2048
+  if (nsw > kHnbMaxStages) nsw = kHnbMaxStages;
+  const size_t smem = fixed + per * nsw;
+  const int64_t chunks = hn_chunks(a.tokens);
+  const dim3 grid(static_cast<unsigned>(chunks < dev.sms ? chunks : dev.sms));
+  auto go = [&](auto kern) -> cudaError_t {
+    cudaError_t e = ensure_smem(kern, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(kern, grid, dim3(kHnbWarps * 32), smem, st, a, nsw);
+  };
   switch (hd) {
-    case 64: return launch_pdl(headnorm_bwd_kernel<64, ROTATE, WITH_K, WITH_V>, grid, block, 0, st, a);
-    case 128: return launch_pdl(headnorm_bwd_kernel<128, ROTATE, WITH_K, WITH_V>, grid, block, 0, st, a);
-    case 256: return launch_pdl(headnorm_bwd_kernel<256, ROTATE, WITH_K, WITH_V>, grid, block, 0, st, a);
+    case 64: return go(headnorm_bwd_kernel<64, ROTATE, WITH_K, WITH_V>);
+    case 128: return go(headnorm_bwd_kernel<128, ROTATE, WITH_K, WITH_V>);
+    case 256: return go(headnorm_bwd_kernel<256, ROTATE, WITH_K, WITH_V>);
     default: return cudaErrorInvalidValue;
   }
 }
 
 inline bool check_heads_bwd(int64_t batch, int64_t seq, int64_t heads, int64_t hd) {
   return check(batch >= 0, "batch must be >= 0") && check(seq >= 1, "seq must be >= 1") &&
-         check(heads >= 1 && heads <= 1024, "heads must be in [1, 1024]") &&
+         check(heads >= 1 && heads * hd <= 2048,
+               "heads * head_dim must be in [1, 2048], got " + std::to_string(heads * hd)) &&
          check(hd == 64 || hd == 128 || hd == 256,
-               "head_dim must be 64, 128 or 256, got " + std::to_string(hd));
+               "head_dim must be 64, 128 or 256, got " + std::to_string(hd)) &&
+         check(finalize_fits(hn_chunks(batch * seq)),
+               "backward supports batch * seq <= " + std::to_string(32768 * kHnbWarps));
 }
 
 static cudaError_t finalize(const HeadNormBwdArgs& a, void* dw0, void* dw1, int nsec, int hd,
                             cudaStream_t st) {
-  const int64_t slots = hn_slots(a.tokens, hd);
-  return launch_pdl(headnorm_bwd_finalize_kernel, dim3((nsec * hd + 127) / 128), dim3(128), 0, st,
-                    static_cast<const float*>(a.part), static_cast<float*>(dw0),
-                    static_cast<float*>(dw1), slots, nsec, hd);
+  FinalizeArgs f{};
+  f.part = a.part;
+  f.n = hn_chunks(a.tokens);
+  f.ncols = nsec * hd;
+  f.seg = hd;
+  f.out[0] = dw0;
+  f.out[1] = dw1;
+  f.bf16_out = 0;
+  if (f.n == 0) {  // no tokens: the gradients are zero
+    cudaError_t e = cudaMemsetAsync(dw0, 0, hd * sizeof(float), st);
+    if (e == cudaSuccess && nsec > 1) e = cudaMemsetAsync(dw1, 0, hd * sizeof(float), st);
+    return e;
+  }
+  return launch_colsum_finalize(f, 1, st);
+}
+
+cudaError_t read_status_headnorm_bwd(int* status) {
+  return cudaMemcpyFromSymbol(status, g_afb_device_status, sizeof(int));
 }
 
 }  // namespace afb

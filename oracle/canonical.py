@@ -141,8 +141,8 @@ def gelu(x_bits: np.ndarray) -> np.ndarray:
 # it fixes the order of the parameter-gradient sums.
 BWD_WARPS = 4
 BWD_ROWS_PER_WARP = 4
-HN_WARPS = 4
-HN_TOK_PER_WARP = 4
+HN_WARPS = 8
+HN_TOK_PER_WARP = 1
 
 
 def adaln_bwd(gh, z, scale, x=None, gate=None, gz=None, eps=1e-6, mode=RNE):

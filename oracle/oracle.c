@@ -348,6 +348,19 @@ void orc_head_norm(const uint16_t* x, const float* w, uint16_t* y, int64_t B, in
 
 /* ------------------------------------------------------------ backward -- */
 
+/* Stride tree over n rows of `cols` floats (rows zero-padded to a power of
+ * two); the result is written to out[0..cols). */
+static void stride_tree_rows(const float* rows, int64_t n, int64_t cols, float* out) {
+  int64_t np = 1;
+  while (np < n) np <<= 1;
+  float* t = (float*)calloc((size_t)(np * cols), sizeof(float));
+  memcpy(t, rows, (size_t)(n * cols) * sizeof(float));
+  for (int64_t h = np / 2; h >= 1; h /= 2)
+    for (int64_t v = 0; v < h; ++v)
+      for (int64_t c = 0; c < cols; ++c) t[v * cols + c] = t[v * cols + c] + t[(v + h) * cols + c];
+  memcpy(out, t, (size_t)cols * sizeof(float));
+  free(t);
+}
 /* src/kernels/adaln.py:133-217.  Per row: mean, rstd of z; xhat = d*rstd;
  * dxh = gh*scale; c1 = sum(dxh)/D; c2 = sum(dxh*xhat)/D;
  * dz = rstd*((dxh - c1) - xhat*c2) (+ gz) -> bf16; dx = bf16(dz*gate).
@@ -355,9 +368,10 @@ void orc_head_norm(const uint16_t* x, const float* w, uint16_t* y, int64_t B, in
  * dgate = sum dz*x) in the canonical order of the CUDA kernel: chunks of
  * `warps * rows_per_warp` rows; in a chunk warp w sums rows w, w+warps, ...;
  * the warp sums combine as a stride tree over warps (pairs w, w + warps/2
- * first), the chunk sums add in increasing chunk order; then bf16.  In
- * INTERP mode the per-row sums are numpy's; the parameter gradients keep the
- * canonical order. */
+ * first), and the chunk sums combine by a stride tree over the chunk index
+ * (zero-padded to a power of two); then bf16.  In INTERP mode the per-row
+ * sums are numpy's; the parameter gradients keep the canonical order. */
+
 void orc_adaln_bwd(const uint16_t* gh, const uint16_t* gz, const uint16_t* z, const uint16_t* x,
                    const uint16_t* gate, const uint16_t* scale, uint16_t* dz_out,
                    uint16_t* dx_out, uint16_t* dgate, uint16_t* dshift, uint16_t* dscale,
@@ -370,10 +384,10 @@ void orc_adaln_bwd(const uint16_t* gh, const uint16_t* gz, const uint16_t* z, co
   float* t1 = (float*)malloc((size_t)D * sizeof(float));
   float* t2 = (float*)malloc((size_t)D * sizeof(float));
   float* wp = (float*)malloc((size_t)warps * nq * D * sizeof(float)); /* warp partials */
+  float* cs = (float*)malloc((size_t)chunks * nq * D * sizeof(float)); /* chunk sums */
   float* tot = (float*)malloc((size_t)nq * D * sizeof(float));
   for (int64_t b = 0; b < B; ++b) {
     const int64_t po = b * D;
-    for (int64_t i = 0; i < nq * D; ++i) tot[i] = 0.0f;
     for (int64_t c = 0; c < chunks; ++c) {
       for (int64_t i = 0; i < (int64_t)warps * nq * D; ++i) wp[i] = 0.0f;
       for (int r = 0; r < rows_per_warp; ++r) {
@@ -417,25 +431,27 @@ void orc_adaln_bwd(const uint16_t* gh, const uint16_t* gz, const uint16_t* z, co
         for (int w = 0; w < span / 2; ++w)
           for (int64_t i = 0; i < nq * D; ++i)
             wp[(int64_t)w * nq * D + i] = wp[(int64_t)w * nq * D + i] + wp[(int64_t)(w + span / 2) * nq * D + i];
-      for (int64_t i = 0; i < nq * D; ++i) tot[i] = tot[i] + wp[i];
+      memcpy(cs + c * nq * D, wp, (size_t)(nq * D) * sizeof(float));
     }
+    stride_tree_rows(cs, chunks, nq * D, tot);
     for (int64_t i = 0; i < D; ++i) {
       dshift[po + i] = orc_f32_to_bf16(tot[i], ROUND_RNE);
       dscale[po + i] = orc_f32_to_bf16(tot[D + i], ROUND_RNE);
       if (has_x) dgate[po + i] = orc_f32_to_bf16(tot[2 * D + i], ROUND_RNE);
     }
   }
-  free(zf); free(t1); free(t2); free(wp); free(tot);
+  free(zf); free(t1); free(t2); free(wp); free(cs); free(tot);
 }
 
 /* src/kernels/rope.py:223-383, :386-436.  Per token and head: undo the
  * rotation of the upstream gradient (da' = da*cos + db*sin,
  * db' = db*cos - da*sin), rstd of the forward input, xhat = x*rstd,
  * u = d'*w, c = sum(u*xhat)/hd, dx = bf16(rstd*(u - xhat*c)); dw += d'*xhat.
- * Weight-gradient order as the CUDA kernel: tokens in chunks of
- * warps * tok_per_warp, warp w takes tokens w, w+warps, ..., lane group g
- * takes heads g, g + hpi, ... (hpi = 32 / (hd/8)); each (chunk, warp, group)
- * slot sums sequentially from zero; slots add in increasing order.
+ * Weight-gradient order as the CUDA kernel: tokens in chunks of `warps`;
+ * per token, lane group g (hpi = 32 / (hd/16) groups) sums heads
+ * g, g + hpi, ... in increasing order from zero and the groups combine as a
+ * stride tree; the token sums of a chunk combine as a stride tree over the
+ * token index; the chunk sums as a stride tree over the chunk index.
  * src/dsrc rows are src_row wide with the normed sections at q_off/k_off
  * (nsec = 1 or 2) and, when dv is given, v at v_off. */
 void orc_headnorm_bwd(const uint16_t* src, int64_t src_row, int64_t q_off, int64_t k_off,
@@ -444,62 +460,67 @@ void orc_headnorm_bwd(const uint16_t* src, int64_t src_row, int64_t q_off, int64
                       uint16_t* dsrc, float* dw0, float* dw1, int64_t tokens, int64_t S,
                       int64_t H, int64_t hd, float eps, int rotate, int nsec, int warps,
                       int tok_per_warp, int mode) {
-  const int64_t half = hd / 2, lph = hd / 8, hpi = 32 / lph;
-  const int64_t chunk_toks = (int64_t)warps * tok_per_warp;
-  const int64_t chunks = (tokens + chunk_toks - 1) / chunk_toks;
+  (void)tok_per_warp;
+  const int64_t half = hd / 2, hpi = 32 / (hd / 16);
+  const int64_t chunks = (tokens + warps - 1) / warps;
+  const int64_t ns = 2 * hd; /* per-token sums, both sections */
   float* x = (float*)malloc((size_t)hd * sizeof(float));
   float* d = (float*)malloc((size_t)hd * sizeof(float));
   float* t = (float*)malloc((size_t)hd * sizeof(float));
-  float* slot = (float*)malloc((size_t)2 * hd * sizeof(float));
-  float* tot = (float*)calloc((size_t)2 * hd, sizeof(float));
-  for (int64_t c = 0; c < chunks; ++c)
-    for (int w = 0; w < warps; ++w)
-      for (int64_t g = 0; g < hpi; ++g) {
-        for (int64_t i = 0; i < 2 * hd; ++i) slot[i] = 0.0f;
-        for (int r = 0; r < tok_per_warp; ++r) {
-          const int64_t tok = c * chunk_toks + (int64_t)r * warps + w;
-          if (tok >= tokens) continue;
-          const int64_t pos = tok % S;
-          for (int sec = 0; sec < nsec; ++sec) {
-            const uint16_t* in = src + tok * src_row + (sec ? k_off : q_off);
-            uint16_t* out = dsrc + tok * src_row + (sec ? k_off : q_off);
-            const uint16_t* go = (sec ? dk : dq) + tok * H * hd;
-            const float* wv = sec ? wk : wq;
-            for (int64_t h = g; h < H; h += hpi) {
-              for (int64_t i = 0; i < hd; ++i) {
-                x[i] = orc_bf16_to_f32(in[h * hd + i]);
-                d[i] = orc_bf16_to_f32(go[h * hd + i]);
+  float* grp = (float*)malloc((size_t)(hpi * ns) * sizeof(float));
+  float* tokp = (float*)malloc((size_t)(warps * ns) * sizeof(float));
+  float* chunkp = (float*)calloc((size_t)((chunks > 0 ? chunks : 1) * ns), sizeof(float));
+  for (int64_t c = 0; c < chunks; ++c) {
+    for (int w = 0; w < warps; ++w) {
+      const int64_t tok = c * warps + w;
+      for (int64_t i = 0; i < hpi * ns; ++i) grp[i] = 0.0f;
+      if (tok < tokens) {
+        const int64_t pos = tok % S;
+        for (int sec = 0; sec < nsec; ++sec) {
+          const uint16_t* in = src + tok * src_row + (sec ? k_off : q_off);
+          uint16_t* out = dsrc + tok * src_row + (sec ? k_off : q_off);
+          const uint16_t* go = (sec ? dk : dq) + tok * H * hd;
+          const float* wv = sec ? wk : wq;
+          for (int64_t h = 0; h < H; ++h) {
+            float* acc = grp + (h % hpi) * ns + sec * hd;
+            for (int64_t i = 0; i < hd; ++i) {
+              x[i] = orc_bf16_to_f32(in[h * hd + i]);
+              d[i] = orc_bf16_to_f32(go[h * hd + i]);
+            }
+            if (rotate)
+              for (int64_t i = 0; i < half; ++i) {
+                const float c0 = cs[pos * half + i], s0 = sn[pos * half + i];
+                const float da = d[i], db = d[i + half];
+                d[i] = (da * c0) + (db * s0);
+                d[i + half] = (db * c0) - (da * s0);
               }
-              if (rotate)
-                for (int64_t i = 0; i < half; ++i) {
-                  const float c0 = cs[pos * half + i], s0 = sn[pos * half + i];
-                  const float da = d[i], db = d[i + half];
-                  d[i] = (da * c0) + (db * s0);
-                  d[i + half] = (db * c0) - (da * s0);
-                }
-              for (int64_t i = 0; i < hd; ++i) t[i] = x[i] * x[i];
-              const float ss = (mode == ROUND_INTERP)
-                                   ? orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)
-                                   : orc_canonical_sum(t, hd, (int)lph);
-              const float rstd = 1.0f / sqrtf(ss / (float)hd + eps);
-              for (int64_t i = 0; i < hd; ++i) t[i] = (d[i] * wv[i]) * (x[i] * rstd);
-              const float cc = ((mode == ROUND_INTERP)
-                                    ? orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)
-                                    : orc_canonical_sum(t, hd, (int)lph)) / (float)hd;
-              for (int64_t i = 0; i < hd; ++i) {
-                const float xh = x[i] * rstd, u = d[i] * wv[i];
-                out[h * hd + i] = orc_f32_to_bf16(rstd * (u - xh * cc), mode);
-                slot[sec * hd + i] = slot[sec * hd + i] + d[i] * xh;
-              }
+            for (int64_t i = 0; i < hd; ++i) t[i] = x[i] * x[i];
+            const float ss = (mode == ROUND_INTERP)
+                                 ? orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)
+                                 : orc_canonical_sum(t, hd, (int)(hd / 8));
+            const float rstd = 1.0f / sqrtf(ss / (float)hd + eps);
+            for (int64_t i = 0; i < hd; ++i) t[i] = (d[i] * wv[i]) * (x[i] * rstd);
+            const float cc = ((mode == ROUND_INTERP)
+                                  ? orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)
+                                  : orc_canonical_sum(t, hd, (int)(hd / 8))) / (float)hd;
+            for (int64_t i = 0; i < hd; ++i) {
+              const float xh = x[i] * rstd, u = d[i] * wv[i];
+              out[h * hd + i] = orc_f32_to_bf16(rstd * (u - xh * cc), mode);
+              acc[i] = acc[i] + d[i] * xh;
             }
           }
-          if (dv) memcpy(dsrc + tok * src_row + v_off, dv + tok * H * hd, (size_t)(H * hd) * 2);
         }
-        for (int64_t i = 0; i < 2 * hd; ++i) tot[i] = tot[i] + slot[i];
+        if (dv) memcpy(dsrc + tok * src_row + v_off, dv + tok * H * hd, (size_t)(H * hd) * 2);
       }
+      stride_tree_rows(grp, hpi, ns, tokp + (int64_t)w * ns); /* over the lane groups */
+    }
+    stride_tree_rows(tokp, warps, ns, chunkp + c * ns); /* over the tokens of the chunk */
+  }
+  float tot[512];
+  stride_tree_rows(chunkp, chunks > 0 ? chunks : 1, ns, tot); /* over the chunks */
   for (int64_t i = 0; i < hd; ++i) {
     dw0[i] = tot[i];
     if (nsec > 1) dw1[i] = tot[hd + i];
   }
-  free(x); free(d); free(t); free(slot); free(tot);
+  free(x); free(d); free(t); free(grp); free(tokp); free(chunkp);
 }

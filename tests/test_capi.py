@@ -41,9 +41,9 @@ def test_workspace_queries():
     # [B][chunks of 16 rows][3][D] fp32
     assert lib.afb_residual_adaln_bwd_workspace(1, 4096, 2048) == 1 * 256 * 3 * 2048 * 4
     assert lib.afb_adaln_bwd_workspace(2, 17, 256) == 2 * 2 * 2 * 256 * 4
-    # [chunks of 16 tokens][4 warps][2 head groups][2][128] fp32
-    assert lib.afb_qkv_norm_rope_bwd_workspace(1, 4096, 16, 128) == 256 * 4 * 2 * 2 * 128 * 4
-    assert lib.afb_head_norm_bwd_workspace(1, 4096, 16, 128) == 256 * 4 * 2 * 1 * 128 * 4
+    # [chunks of 8 tokens][sections][128] fp32
+    assert lib.afb_qkv_norm_rope_bwd_workspace(1, 4096, 16, 128) == 512 * 2 * 128 * 4
+    assert lib.afb_head_norm_bwd_workspace(1, 4096, 16, 128) == 512 * 1 * 128 * 4
 
 
 def test_backward_rejects_small_workspace():
