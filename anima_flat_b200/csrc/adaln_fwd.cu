@@ -10,16 +10,28 @@
 //   bf16 output:  h = bf16(y)
 //   FP8 output:   s = max(max|y|, 1e-12) / 448;  q = e4m3(clamp(y / s, +-448))
 //
-// Layout: persistent CTAs, one per SM, of kAdalnWarps warps.  Warp g of the
-// grid owns rows g, g + W, g + 2W, ... (W = warps in the grid) and keeps a
-// private ring of `nsw` shared-memory stages; lane 0 streams each row's res
-// (and x) into a stage with bulk copies (TMA engine) that complete on the
-// stage's mbarrier, so up to nsw rows per warp are in flight while the warp
-// computes.  A row moves from its stage into registers (lane l holds the
-// 16-byte vectors v = l + 32*c, c < NC), the stage is refilled at once, and
-// z and h (or q) are written straight from registers.  z = res + gate*x uses
-// packed bf16x2 arithmetic; the statistics and the modulation use packed
-// fp32x2 adds/subs under the contraction rule of afb_device.cuh.
+// Layout: persistent CTAs, one per SM, of kAdalnPairs warp pairs.  CTA c owns
+// the contiguous rows [c*R/G, (c+1)*R/G) (R rows, G CTAs: every SM gets the
+// same share within one row), and pair p of it the rows p, p + kAdalnPairs, ...
+// of that range.  Each pair keeps a private ring of `nsw` shared-memory stages;
+// its leader lane streams each row's res (and x) into a stage with bulk copies
+// (TMA engine) that complete on the stage's mbarrier, so up to nsw rows per
+// pair are in flight while the pair computes.  The modulation vectors of the
+// (at most two) batch entries a CTA's rows belong to are bulk-copied into
+// shared memory first, ahead of the row stream, so no per-row global load
+// waits behind it; a CTA whose rows span more batch entries (short sequences)
+// reads them from global memory instead.  Both warps of a pair work on the same row: with
+// NC = D/256 vectors of 8 elements per lane, warp h holds the vectors
+// v = lane + 32*c for c = 2i + h (i < NC/2), so a row costs each warp half the
+// instructions and half the latency.  The canonical sums keep their order:
+// every level of the vector stride tree but the last pairs vectors of equal
+// parity, inside one warp; the last level adds the two warps' vectors through
+// shared memory (pair_canonical_sum2).  z and h (or q) are written straight
+// from registers.  z = res + gate*x uses packed bf16x2 arithmetic; the
+// statistics and the modulation use packed fp32x2 adds/subs under the
+// contraction rule of afb_device.cuh.  In FP8 mode y stays in registers
+// between the row max and the codes, and y / s is the product by RN(1/s)
+// wherever that provably gives the IEEE quotient's code (e4m3_quot8).
 #include "afb_device.cuh"
 #include "afb_launch.h"
 
@@ -41,34 +53,130 @@ struct AdalnArgs {
   float eps;
 };
 
-constexpr int kAdalnWarps = 8;
+constexpr int kAdalnPairs = 8;
+constexpr int kAdalnWarps = 2 * kAdalnPairs;
 constexpr int kAdalnMaxStages = 4;
+// Per pair: two exchange buffers (one per sum of a row) of 2 warps x 4 pairs
+// of fp32 x 32 lanes, then two floats for the FP8 row max (padded to 16 B).
+constexpr size_t kAdalnXchF2 = 2 * 2 * 4 * 32;
+constexpr size_t kAdalnPairXchBytes = kAdalnXchF2 * sizeof(f2_t) + 4 * sizeof(float);
+// Modulation slots: the scale, shift (and gate) rows of up to two batch
+// entries, bf16 in shared memory.  Slot layout: [scale D][shift D][gate D].
+// (Widening them to fp32 once per CTA saves the per-row unpacking but doubles
+// the shared-memory bytes read per row, and measured slower.)
+constexpr int kAdalnModSlots = 2;
+__host__ __device__ constexpr size_t adaln_slot_bytes(int64_t dim, bool has_x) {
+  return static_cast<size_t>(dim) * (has_x ? 6 : 4);
+}
+__host__ __device__ constexpr size_t adaln_mod_bytes(int64_t dim, bool has_x) {
+  return kAdalnModSlots * adaln_slot_bytes(dim, has_x);
+}
+
+// Canonical sum (P = 32) of a row held by the two warps of a pair.  val(i, j)
+// is the fp32 pair (2j, 2j+1) of the lane's i-th vector (vector index
+// c = 2i + h when SPLIT, else i).  The stride tree over the NH local vectors
+// runs in registers (first level fused with val); with SPLIT the last level
+// adds the partner warp's vector from `xch` ([warp][pair][lane]) after the
+// pair barrier.  Both warps return the same sum.
+template <int NH, bool SPLIT, typename F>
+__device__ __forceinline__ float pair_canonical_sum2(F val, f2_t* xch, int h, int lane, int bar_id) {
+  constexpr int H = NH > 1 ? NH / 2 : 1;
+  f2_t p[H][4];
+#pragma unroll
+  for (int i = 0; i < H; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (NH > 1) {
+        p[i][j] = add2(val(i, j), val(i + H, j));
+      } else {
+        p[i][j] = val(i, j);
+      }
+    }
+  }
+#pragma unroll
+  for (int s = H / 2; s >= 1; s >>= 1) {
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[i][j] = add2(p[i][j], p[i + s][j]);
+    }
+  }
+  if constexpr (SPLIT) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xch[(h * 4 + j) * 32 + lane] = p[0][j];
+    named_bar_sync(bar_id, 64);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) p[0][j] = add2(p[0][j], xch[((h ^ 1) * 4 + j) * 32 + lane]);
+  }
+  const f2_t q = add2(add2(p[0][0], p[0][2]), add2(p[0][1], p[0][3]));
+  float r = __fadd_rn(f2lo(q), f2hi(q));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) r = __fadd_rn(r, __shfl_xor_sync(kFull, r, o));
+  return r;
+}
 
 // EXACT: dim == 256 * NC, so every lane owns NC full vectors (no masking).
+// use_smods: the launch reserved shared memory for the modulation slots.
 template <int NC, bool HAS_X, bool FP8, bool EXACT>
 __global__ void __launch_bounds__(kAdalnWarps * 32, 1)
-adaln_fwd_kernel(const AdalnArgs a, const int nsw) {
+adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods) {
+  // SPLIT: the pair divides each lane's vectors; for NC == 1 both warps hold
+  // the single vector and warp 0 writes the outputs.
+  constexpr bool SPLIT = NC >= 2;
+  constexpr int NH = SPLIT ? NC / 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  const int pair = warp >> 1;
+  const int h = warp & 1;
+  const int bar_id = 1 + pair;
+  const bool leader = h == 0 && lane == 0;
+  const bool writer = SPLIT || h == 0;
   const int D = EXACT ? NC * 256 : a.dim;
   const uint32_t row_bytes = static_cast<uint32_t>(D) * 2u;
   const uint32_t stage_bytes = (HAS_X ? 2u : 1u) * row_bytes;
-  uint8_t* ring = smem + static_cast<size_t>(warp) * nsw * stage_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kAdalnWarps) * nsw * stage_bytes) +
-                   warp * nsw;
-  if (lane == 0) {
+  const size_t slot_bytes = adaln_slot_bytes(D, HAS_X);
+  const size_t ring_all = static_cast<size_t>(kAdalnPairs) * nsw * stage_bytes;
+  uint8_t* ring = smem + static_cast<size_t>(pair) * nsw * stage_bytes;
+  uint8_t* xbase = smem + ring_all + static_cast<size_t>(pair) * kAdalnPairXchBytes;
+  f2_t* xch = reinterpret_cast<f2_t*>(xbase);
+  float* xmax = reinterpret_cast<float*>(xbase + kAdalnXchF2 * sizeof(f2_t));
+  uint8_t* mods = smem + ring_all + kAdalnPairs * kAdalnPairXchBytes;
+  uint64_t* bars0 = reinterpret_cast<uint64_t*>(mods + (use_smods ? adaln_mod_bytes(D, HAS_X) : 0));
+  uint64_t* bars = bars0 + pair * nsw;
+  uint64_t* modbar = bars0 + kAdalnPairs * nsw;
+
+  // This CTA's rows, and the batch entries they belong to.
+  const int64_t r0 = a.rows * blockIdx.x / gridDim.x;
+  const int64_t r1 = a.rows * (blockIdx.x + 1) / gridDim.x;
+  const int64_t b_lo = r1 > r0 ? r0 / a.seq : 0;
+  const int64_t b_hi = r1 > r0 ? (r1 - 1) / a.seq : 0;
+  const bool smods = use_smods && r1 > r0 && b_hi - b_lo < kAdalnModSlots;
+  const int nb = static_cast<int>(b_hi - b_lo + 1);
+  if (leader) {
     for (int s = 0; s < nsw; ++s) mbar_init(smem_addr(&bars[s]), 1);
+    if (pair == 0) mbar_init(smem_addr(modbar), 1);
     fence_mbar_init();
   }
-  __syncwarp();
+  __syncthreads();  // barriers initialised before anyone waits on them
   pdl_wait();
   pdl_trigger();
+  if (smods && threadIdx.x == 0) {
+    // The modulation rows go first, ahead of every row stage.
+    mbar_arrive_expect_tx(smem_addr(modbar), static_cast<uint32_t>(nb * (HAS_X ? 3 : 2)) * row_bytes);
+    for (int k = 0; k < nb; ++k) {
+      const int64_t pb = (b_lo + k) * D;
+      uint8_t* slot = mods + k * slot_bytes;
+      bulk_g2s(smem_addr(slot), a.scale + pb, row_bytes, smem_addr(modbar));
+      bulk_g2s(smem_addr(slot + 2 * D), a.shift + pb, row_bytes, smem_addr(modbar));
+      if (HAS_X) bulk_g2s(smem_addr(slot + 4 * D), a.gate + pb, row_bytes, smem_addr(modbar));
+    }
+  }
+  if (smods) __syncthreads();
 
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kAdalnWarps + warp;
-  const int64_t nw = static_cast<int64_t>(gridDim.x) * kAdalnWarps;
-  auto issue = [&](int64_t j) {  // lane 0: stream row gw + j*nw into stage j % nsw
-    const int64_t row = gw + j * nw;
+  auto row_of = [&](int64_t j) { return r0 + pair + j * kAdalnPairs; };
+  auto issue = [&](int64_t j) {  // leader: stream row row_of(j) into stage j % nsw
+    const int64_t row = row_of(j);
     const int s = static_cast<int>(j % nsw);
     uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
@@ -76,52 +184,73 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw) {
     bulk_g2s(smem_addr(st), a.res + row * D, row_bytes, bar);
     if (HAS_X) bulk_g2s(smem_addr(st + row_bytes), a.x + row * D, row_bytes, bar);
   };
-  if (lane == 0) {
-    for (int j = 0; j < nsw && gw + j * nw < a.rows; ++j) issue(j);
+  if (leader) {
+    for (int j = 0; j < nsw && row_of(j) < r1; ++j) issue(j);
   }
-  auto ok = [&](int c) { return EXACT || (lane + 32 * c) * 8 < D; };
-  auto col = [&](int c) { return (lane + 32 * c) * 8; };
+  auto col = [&](int i) { return (lane + 32 * (SPLIT ? 2 * i + h : i)) * 8; };
+  auto ok = [&](int i) { return EXACT || col(i) < D; };
 
-  for (int64_t j = 0; gw + j * nw < a.rows; ++j) {
-    const int64_t row = gw + j * nw;
+  // A wait that gives up (never expected) marks the warp dead: it keeps taking
+  // the pair's barriers but stores nothing and issues no copy, and the leader
+  // drains its copies in flight before the CTA exits.
+  bool dead = false;
+  int64_t jdead = 0;
+  if (smods && !mbar_wait(smem_addr(modbar), 0)) dead = true;
+  // fp32 pairs (2j, 2j+1) of modulation row v (0 scale, 1 shift) of batch
+  // entry b at columns c .. c+7.
+  auto mod8 = [&](int v, int64_t b, int c, f2_t (&m)[4]) {
+    const uint4 w = smods ? lds16(mods + static_cast<size_t>(b - b_lo) * slot_bytes + v * 2 * D + c * 2)
+                          : ld_keep((v == 0 ? a.scale : a.shift) + b * D + c);
+    m[0] = bf2f2(w.x);
+    m[1] = bf2f2(w.y);
+    m[2] = bf2f2(w.z);
+    m[3] = bf2f2(w.w);
+  };
+  auto gate8 = [&](int64_t b, int c) {
+    return smods ? lds16(mods + static_cast<size_t>(b - b_lo) * slot_bytes + 4 * D + c * 2)
+                 : ld_keep(a.gate + b * D + c);
+  };
+
+  for (int64_t j = 0; row_of(j) < r1; ++j) {
+    const int64_t row = row_of(j);
     const int s = static_cast<int>(j % nsw);
     const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-    if (!mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
-      // Never expected: drain this warp's other copies (bounded), then stop.
-      for (int64_t k = j + 1; k < j + nsw && gw + k * nw < a.rows; ++k)
-        mbar_wait(smem_addr(&bars[k % nsw]), static_cast<uint32_t>((k / nsw) & 1));
-      return;
+    if (!dead && !mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
+      dead = true;
+      jdead = j;
     }
+    const bool store = writer && !dead;
     const int64_t b = row / a.seq;
     const int64_t base = row * D;
-    const int64_t pbase = b * D;
 
-    // stage -> registers; z = bf16(res + bf16(gate * x)) in packed bf16x2
-    uint4 zv[NC];
+    // stage -> registers; z = bf16(res + bf16(gate * x)) in packed bf16x2;
+    // zf = fp32(z) (zero for masked vectors), later d = z - mean in place.
+    f2_t zf[NH][4];
     {
-      uint4 xv[NC];
+      uint4 zv[NH];
+      uint4 xv[NH];
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        zv[c] = ok(c) ? lds16(st + col(c) * 2) : make_uint4(0, 0, 0, 0);
-        if (HAS_X) xv[c] = ok(c) ? lds16(st + row_bytes + col(c) * 2) : make_uint4(0, 0, 0, 0);
-      }
-      __syncwarp();
-      if (lane == 0 && gw + (j + nsw) * nw < a.rows) {
-        fence_proxy_async_smem();
-        issue(j + nsw);
+      for (int i = 0; i < NH; ++i) {
+        zv[i] = ok(i) ? lds16(st + col(i) * 2) : make_uint4(0, 0, 0, 0);
+        if (HAS_X) xv[i] = ok(i) ? lds16(st + row_bytes + col(i) * 2) : make_uint4(0, 0, 0, 0);
       }
       if (HAS_X) {
 #pragma unroll
-        for (int c = 0; c < NC; ++c) {
-          if (ok(c)) {
-            const uint4 g = ld_keep(a.gate + pbase + col(c));
-            zv[c].x = badd2(zv[c].x, bmul2(g.x, xv[c].x));
-            zv[c].y = badd2(zv[c].y, bmul2(g.y, xv[c].y));
-            zv[c].z = badd2(zv[c].z, bmul2(g.z, xv[c].z));
-            zv[c].w = badd2(zv[c].w, bmul2(g.w, xv[c].w));
-            st16(a.z + base + col(c), zv[c]);
+        for (int i = 0; i < NH; ++i) {
+          if (ok(i)) {
+            const uint4 g = gate8(b, col(i));
+            zv[i].x = badd2(zv[i].x, bmul2(g.x, xv[i].x));
+            zv[i].y = badd2(zv[i].y, bmul2(g.y, xv[i].y));
+            zv[i].z = badd2(zv[i].z, bmul2(g.z, xv[i].z));
+            zv[i].w = badd2(zv[i].w, bmul2(g.w, xv[i].w));
+            if (store) st16(a.z + base + col(i), zv[i]);
           }
         }
+      }
+#pragma unroll
+      for (int i = 0; i < NH; ++i) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) zf[i][jj] = bf2f2(word(zv[i], jj));
       }
     }
 
@@ -130,77 +259,105 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw) {
     auto div_d = [&](float x) {
       return EXACT ? __fmul_rn(x, 1.0f / (NC * 256)) : __fdiv_rn(x, static_cast<float>(D));
     };
-    const float mean = div_d(
-        warp_canonical_sum2_fn<NC>([&](int c, int jj) { return bf2f2(word(zv[c], jj)); }));
+    const float mean = div_d(pair_canonical_sum2<NH, SPLIT>(
+        [&](int i, int jj) { return zf[i][jj]; }, xch, h, lane, bar_id));
+    // Both warps have read the stage (the pair barrier above): refill it.
+    if (!SPLIT) named_bar_sync(bar_id, 64);
+    if (leader && !dead && row_of(j + nsw) < r1) {
+      fence_proxy_async_smem();
+      issue(j + nsw);
+    }
     const f2_t mm = f2(mean, mean);
-    const float var = div_d(warp_canonical_sum2_fn<NC>([&](int c, int jj) {
-      const f2_t d = ok(c) ? sub2(bf2f2(word(zv[c], jj)), mm) : 0ull;
-      return mul2_noc(d, d);
-    }));
+#pragma unroll
+    for (int i = 0; i < NH; ++i) {
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) zf[i][jj] = ok(i) ? sub2(zf[i][jj], mm) : 0ull;
+    }
+    const float var = div_d(pair_canonical_sum2<NH, SPLIT>(
+        [&](int i, int jj) { return mul2_noc(zf[i][jj], zf[i][jj]); }, xch + 2 * 4 * 32, h, lane,
+        bar_id));
     const float rstd = canonical_rstd(var, a.eps);
     const f2_t rr = f2(rstd, rstd);
-    // y = ((z - mean) * rstd) * scale + shift for elements (2jj, 2jj+1) of vector c
-    auto ypair = [&](int c, int jj, const uint4& scv, const uint4& shv) {
-      const f2_t d = sub2(bf2f2(word(zv[c], jj)), mm);
-      return add2(mul2_noc(mul2(d, rr), bf2f2(word(scv, jj))), bf2f2(word(shv, jj)));
+    // y = ((z - mean) * rstd) * scale + shift for elements (2jj, 2jj+1) of vector i
+    auto ypair = [&](int i, int jj, const f2_t (&sc)[4], const f2_t (&sh)[4]) {
+      return add2(mul2_noc(mul2(zf[i][jj], rr), sc[jj]), sh[jj]);
     };
 
     if (!FP8) {
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        if (ok(c)) {
-          const uint4 scv = ld_keep(a.scale + pbase + col(c));
-          const uint4 shv = ld_keep(a.shift + pbase + col(c));
+      for (int i = 0; i < NH; ++i) {
+        if (ok(i) && store) {
+          f2_t sc[4], sh[4];
+          mod8(0, b, col(i), sc);
+          mod8(1, b, col(i), sh);
           uint4 o;
-          o.x = f2bf2(ypair(c, 0, scv, shv));
-          o.y = f2bf2(ypair(c, 1, scv, shv));
-          o.z = f2bf2(ypair(c, 2, scv, shv));
-          o.w = f2bf2(ypair(c, 3, scv, shv));
-          st16(a.h + base + col(c), o);
+          o.x = f2bf2(ypair(i, 0, sc, sh));
+          o.y = f2bf2(ypair(i, 1, sc, sh));
+          o.z = f2bf2(ypair(i, 2, sc, sh));
+          o.w = f2bf2(ypair(i, 3, sc, sh));
+          st16(a.h + base + col(i), o);
         }
       }
     } else {
+      // y is computed once and kept in registers for the amax and the codes.
+      float y[NH][8];
       float amax = 0.0f;
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        if (ok(c)) {
-          const uint4 scv = ld_keep(a.scale + pbase + col(c));
-          const uint4 shv = ld_keep(a.shift + pbase + col(c));
+      for (int i = 0; i < NH; ++i) {
+        if (ok(i)) {
+          f2_t sc[4], sh[4];
+          mod8(0, b, col(i), sc);
+          mod8(1, b, col(i), sh);
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
-            const f2_t y = ypair(c, jj, scv, shv);
-            amax = fmaxf(amax, fmaxf(fabsf(f2lo(y)), fabsf(f2hi(y))));
+            const f2_t v = ypair(i, jj, sc, sh);
+            y[i][2 * jj] = f2lo(v);
+            y[i][2 * jj + 1] = f2hi(v);
+            amax = fmaxf(amax, fmaxf(fabsf(y[i][2 * jj]), fabsf(y[i][2 * jj + 1])));
           }
         }
       }
       amax = warp_max(amax);
-      const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
-#pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        if (ok(c)) {
-          const uint4 scv = ld_keep(a.scale + pbase + col(c));
-          const uint4 shv = ld_keep(a.shift + pbase + col(c));
-          float qf[8];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const f2_t y = ypair(c, jj, scv, shv);
-            qf[2 * jj] = fminf(fmaxf(__fdiv_rn(f2lo(y), sc), -448.0f), 448.0f);
-            qf[2 * jj + 1] = fminf(fmaxf(__fdiv_rn(f2hi(y), sc), -448.0f), 448.0f);
-          }
-          st8(a.q + base + col(c), e4m3x8(qf));
-        }
+      if (SPLIT) {
+        if (lane == 0) xmax[h] = amax;
+        named_bar_sync(bar_id, 64);
+        amax = fmaxf(xmax[0], xmax[1]);
       }
-      if (lane == 0) a.s[row] = sc;
+      const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
+      const float rc = __fdiv_rn(1.0f, sc);
+#pragma unroll
+      for (int i = 0; i < NH; ++i) {
+        if (ok(i) && store) st8(a.q + base + col(i), e4m3_quot8(y[i], sc, rc));
+      }
+      if (leader && !dead) a.s[row] = sc;
     }
+  }
+  if (leader && dead) {
+    // Drain the copies issued before the failed wait (bounded waits).
+    for (int64_t k = jdead; k < jdead + nsw && row_of(k) < r1; ++k)
+      mbar_wait(smem_addr(&bars[k % nsw]), static_cast<uint32_t>((k / nsw) & 1));
+    if (pair == 0 && smods) mbar_wait(smem_addr(modbar), 0);
   }
 }
 
-// Stages per warp that fit the shared-memory budget (at least one).
-static int adaln_stages(int64_t dim, bool has_x, size_t smem_limit) {
-  const size_t stage = (has_x ? 2 : 1) * static_cast<size_t>(dim) * 2;
-  const size_t per = kAdalnWarps * (stage + sizeof(uint64_t));
-  const int n = static_cast<int>(smem_limit / per);
-  return n < 1 ? 1 : (n > kAdalnMaxStages ? kAdalnMaxStages : n);
+// Launch plan: stages per pair, and whether the modulation slots fit in
+// shared memory next to at least one stage per pair.
+struct AdalnPlan {
+  int nsw;
+  int smods;
+  size_t smem;
+};
+static AdalnPlan adaln_plan(int64_t dim, bool has_x, size_t limit) {
+  const size_t per = kAdalnPairs * ((has_x ? 2 : 1) * static_cast<size_t>(dim) * 2 + sizeof(uint64_t));
+  const size_t xch = kAdalnPairs * kAdalnPairXchBytes + sizeof(uint64_t);
+  const size_t mods = adaln_mod_bytes(dim, has_x);
+  AdalnPlan p{};
+  p.smods = xch + mods + per <= limit;
+  const size_t fixed = xch + (p.smods ? mods : 0);
+  const int n = limit > fixed ? static_cast<int>((limit - fixed) / per) : 0;
+  p.nsw = n < 1 ? 1 : (n > kAdalnMaxStages ? kAdalnMaxStages : n);
+  p.smem = fixed + p.nsw * per;
+  return p;
 }
 
 template <bool HAS_X, bool FP8>
@@ -209,16 +366,14 @@ static cudaError_t launch_adaln(const AdalnArgs& a, cudaStream_t st) {
   if (dev.error != cudaSuccess) return dev.error;
   const int nc = row_chunks(a.dim);
   const bool exact = a.dim == 256 * nc;
-  const int nsw = adaln_stages(a.dim, HAS_X, dev.max_smem_optin);
-  const size_t smem = static_cast<size_t>(kAdalnWarps) * nsw *
-                      ((HAS_X ? 2 : 1) * static_cast<size_t>(a.dim) * 2 + sizeof(uint64_t));
-  const int64_t want = (a.rows + kAdalnWarps - 1) / kAdalnWarps;
+  const AdalnPlan plan = adaln_plan(a.dim, HAS_X, dev.max_smem_optin);
+  const int64_t want = (a.rows + kAdalnPairs - 1) / kAdalnPairs;
   const dim3 grid(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
   const dim3 block(kAdalnWarps * 32);
   auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = ensure_smem(kern, smem);
+    cudaError_t e = ensure_smem(kern, plan.smem);
     if (e != cudaSuccess) return e;
-    return launch_pdl(kern, grid, block, smem, st, a, nsw);
+    return launch_pdl(kern, grid, block, plan.smem, st, a, plan.nsw, plan.smods);
   };
 #define AFB_LAUNCH_ADALN(NC)                                            \
   return exact ? go(adaln_fwd_kernel<NC, HAS_X, FP8, true>) \

@@ -124,6 +124,38 @@ __device__ __forceinline__ uint2 e4m3x8(const float (&f)[8]) {
   return r;
 }
 
+// Whether the e4m3 code of q = RN(y * RN(1/s)) is certainly the code of the
+// correctly rounded quotient Q = RN(y / s).  RN(1/s) has relative error at
+// most 2^-24, so |y * RN(1/s) - y/s| < 1 ulp and |q - Q| <= 1 ulp.  For
+// |q| >= 2^-6 (the e4m3 normal range) e4m3 keeps 3 of the 23 fp32 mantissa
+// bits, and its rounding midpoints are the values whose low 20 mantissa bits
+// are 0x80000; q and Q round alike unless q lies within 1 ulp of one.  The
+// test rejects a 2-ulp window around each midpoint, everything below 2^-6
+// (the e4m3 subnormal grid), and NaN.
+__device__ __forceinline__ bool e4m3_code_settled(float q) {
+  const uint32_t u = __float_as_uint(q);
+  return ((u - 0x7fffeu) & 0xfffffu) > 4u && fabsf(q) >= 0x1p-6f;
+}
+
+// e4m3 codes of clamp(RN(y[k] / s), +-448): the product by r = RN(1/s) when
+// every code of the vector is settled, else the IEEE quotient.
+__device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, float r) {
+  float q[8];
+  bool settled = true;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    q[k] = __fmul_rn(y[k], r);
+    settled = settled && e4m3_code_settled(q[k]);
+  }
+  if (!settled) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) q[k] = __fdiv_rn(y[k], s);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) q[k] = fminf(fmaxf(q[k], -448.0f), 448.0f);
+  return e4m3x8(q);
+}
+
 // ---------------------------------------------------------------------------
 // Canonical sums.
 // ---------------------------------------------------------------------------
@@ -251,6 +283,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ uint4 lds16(const void* p) {
   return *reinterpret_cast<const uint4*>(p);
 }
+// Named CTA barrier `id` (1..15) over `threads` threads (a multiple of 32);
+// orders the participants' shared-memory accesses like __syncthreads.
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // Packed arithmetic.  Blackwell executes two IEEE fp32 operations per
@@ -264,7 +301,9 @@ __device__ __forceinline__ uint4 lds16(const void* p) {
 // So packed f32x2 is used only for adds/subs, for a sub feeding a multiply
 // and for a multiply feeding a multiply; every product that is then added
 // (squares in the variance, the scale product before + shift) is formed with
-// scalar __fmul_rn.  For bf16 operands,
+// scalar __fmul_rn.  A packed fma.rn.f32x2 with a -0 addend (exactly the
+// rounded product) is folded into a following packed add the same way
+// (observed: up to 30% of results differ), so it is no way around the rule.  For bf16 operands,
 // add.rn.bf16x2(res, mul.rn.bf16x2(g, x)) equals bf16(fp32(res + bf16(g*x))):
 // g*x of two bf16 is exact in fp32, and when res and the product are 17 or
 // more binades apart the fp32 sum rounds to res's bf16 neighbourhood either

@@ -10,8 +10,9 @@
 // one 16-byte FP8 store per chunk.  The amax is a max, so the order of the
 // reduction does not matter.
 //
-// Without GELU every operation is IEEE (q = y / s by division), so codes and
-// scales are exact.  With GELU the per-element work would make the kernel
+// Without GELU the codes and scales are exact: q = y / s is the product by
+// RN(1/s) where that provably gives the code of the IEEE quotient, and the
+// IEEE division elsewhere (e4m3_quot8).  With GELU the per-element work would make the kernel
 // compute-bound, so the codes use fast_gelu() and y * (1 / s); the scale stays
 // exact: every element whose fast value lies within the fast_gelu error bound
 // of the row's fast amax is recomputed with canonical_gelu() and the exact
@@ -73,6 +74,7 @@ rowquant_kernel(const RowquantArgs a) {
 #pragma unroll
     for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(y[c][k]));
   }
+  const float lamax = amax;
 
   // Group-wide max.  Padding elements are zero and leave the max unchanged.
   auto group_max = [&](float v) {
@@ -90,17 +92,20 @@ rowquant_kernel(const RowquantArgs a) {
   amax = group_max(amax);
 
   if (GELU) {
-    // Exact amax over the candidates (see the file comment).
+    // Exact amax over the candidates (see the file comment).  A thread whose
+    // own fast maximum is below the threshold holds no candidate.
     const float margin = __fmaf_rn(amax, 0x1p-11f, 0x1p-19f);
     const float thresh = amax - margin;
     float exact = 0.0f;
+    if (lamax >= thresh) {
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) {
+      for (int c = 0; c < CPL; ++c) {
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        if (fabsf(y[c][k]) >= thresh) {
-          const float xk = unpack_at(xv[c][k >> 3], k & 7);
-          exact = fmaxf(exact, fabsf(canonical_gelu_call(xk)));
+        for (int k = 0; k < 16; ++k) {
+          if (fabsf(y[c][k]) >= thresh) {
+            const float xk = unpack_at(xv[c][k >> 3], k & 7);
+            exact = fmaxf(exact, fabsf(canonical_gelu_call(xk)));
+          }
         }
       }
     }
@@ -117,13 +122,22 @@ rowquant_kernel(const RowquantArgs a) {
       float lo[8], hi[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float vlo = GELU ? __fmul_rn(y[c][k], r) : __fdiv_rn(y[c][k], s);
-        const float vhi = GELU ? __fmul_rn(y[c][k + 8], r) : __fdiv_rn(y[c][k + 8], s);
-        lo[k] = fminf(fmaxf(vlo, -448.0f), 448.0f);
-        hi[k] = fminf(fmaxf(vhi, -448.0f), 448.0f);
+        lo[k] = y[c][k];
+        hi[k] = y[c][k + 8];
       }
-      const uint2 plo = e4m3x8(lo);
-      const uint2 phi = e4m3x8(hi);
+      uint2 plo, phi;
+      if (GELU) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          lo[k] = fminf(fmaxf(__fmul_rn(lo[k], r), -448.0f), 448.0f);
+          hi[k] = fminf(fmaxf(__fmul_rn(hi[k], r), -448.0f), 448.0f);
+        }
+        plo = e4m3x8(lo);
+        phi = e4m3x8(hi);
+      } else {
+        plo = e4m3_quot8(lo, s, r);
+        phi = e4m3_quot8(hi, s, r);
+      }
       st16(a.q + base + e, make_uint4(plo.x, plo.y, phi.x, phi.y));
     }
   }

@@ -42,8 +42,10 @@ def dev(a, cuda_dev):
     return from_bits(a, cuda_dev)
 
 
+# (64, 1, 2048) and (40, 3, 1024): CTAs whose rows span more than two batch
+# entries read the modulation from global memory instead of shared memory.
 ADALN_SHAPES = [(1, 1, 2048), (2, 3, 2048), (1, 4096, 2048), (2, 37, 1024), (3, 5, 256),
-                (1, 7, 4096), (1, 9, 8), (2, 11, 2040), (1, 3, 520)]
+                (1, 7, 4096), (1, 9, 8), (2, 11, 2040), (1, 3, 520), (64, 1, 2048), (40, 3, 1024)]
 
 
 @pytest.mark.parametrize("B,S,D", ADALN_SHAPES)
@@ -68,7 +70,7 @@ def test_adaln_bit_exact(B, S, D, cuda_dev):
 
 
 @pytest.mark.parametrize("B,S,D", [(1, 1, 2048), (2, 4096, 2048), (2, 37, 1024), (3, 5, 256),
-                                   (1, 7, 4096), (2, 11, 2040)])
+                                   (1, 7, 4096), (2, 11, 2040), (64, 1, 2048), (40, 3, 1024)])
 @pytest.mark.parametrize("has_x", [True, False])
 def test_adaln_fp8_bit_exact(B, S, D, has_x, cuda_dev):
     r = rng(B * 3000 + S + D + has_x)
@@ -91,6 +93,50 @@ def test_adaln_fp8_bit_exact(B, S, D, has_x, cuda_dev):
 def test_rowquant_bit_exact(rows, K, cuda_dev):
     r = rng(rows + K)
     x = act(r, (1, rows, K), 0.01)
+    q, s = afb.rowquant(dev(x, cuda_dev), gelu=False)
+    oq, os_ = C.rowquant(x)
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), os_.view(np.uint32))
+    np.testing.assert_array_equal(to_bits(q), oq)
+
+
+def _midpoint_rows(K: int) -> np.ndarray:
+    """Rows whose quotients y / s sit on and next to e4m3 rounding midpoints.
+
+    Row amax A in {1344, 2240, 3136, 448, 1000} gives s = A/448 in {3, 5, 7,
+    1, RN(1000/448)}; for the integer s, x = s*M is exact in bf16 for every
+    e4m3 midpoint M (4 significant bits), so x / s is exactly a tie, where
+    x * RN(1/s) can round to the wrong side.  Each row also holds the bf16
+    neighbours of those x, tiny values below the e4m3 normal range, and
+    signed zeros."""
+    mids = []
+    for e in range(-6, 9):
+        for m in range(8):
+            v = (1.0 + (2 * m + 1) / 16.0) * 2.0 ** e
+            if v < 448.0:
+                mids.append(v)
+    mids = np.array(mids, dtype=np.float32)
+    rows = []
+    for amax in (1344.0, 2240.0, 3136.0, 448.0, 1000.0):
+        s = np.float32(amax) / np.float32(448.0)
+        x = (mids * s).astype(np.float32)
+        xb = torch.from_numpy(x).to(torch.bfloat16)
+        up = torch.nextafter(xb, torch.full_like(xb, float("inf")))
+        dn = torch.nextafter(xb, torch.full_like(xb, float("-inf")))
+        vals = torch.cat([xb, up, dn, -xb, -up]).float().numpy()
+        tiny = np.array([1e-6, -1e-6, 3e-5 * amax, -2e-5 * amax, 0.0, -0.0], dtype=np.float32)
+        row = np.concatenate([vals, tiny, np.array([amax], dtype=np.float32)])
+        row = np.resize(row, K)
+        row[-1] = amax
+        rows.append(row)
+    return bf_bits(np.stack(rows)[None])
+
+
+@pytest.mark.parametrize("K", [2048, 8192])
+def test_rowquant_codes_at_e4m3_midpoints(K, cuda_dev):
+    """The exact rowquant path settles codes from y * RN(1/s) only away from
+    e4m3 ties; on and next to ties its codes must still equal the IEEE
+    quotient's (bit-exact against the oracle, signed zeros included)."""
+    x = _midpoint_rows(K)
     q, s = afb.rowquant(dev(x, cuda_dev), gelu=False)
     oq, os_ = C.rowquant(x)
     np.testing.assert_array_equal(to_bits(s).view(np.uint32), os_.view(np.uint32))
