@@ -55,7 +55,7 @@ struct AdalnArgs {
 
 constexpr int kAdalnPairs = 8;
 constexpr int kAdalnWarps = 2 * kAdalnPairs;
-constexpr int kAdalnMaxStages = 4;
+constexpr int kAdalnMaxStages = 2;  // more stages delay each pair's first row behind the others' copies
 // Per pair: two exchange buffers (one per sum of a row) of 2 warps x 4 pairs
 // of fp32 x 32 lanes, then two floats for the FP8 row max (padded to 16 B).
 constexpr size_t kAdalnXchF2 = 2 * 2 * 4 * 32;

@@ -11,17 +11,22 @@
 // qkv rows are [q | k | v], each heads*hd wide (rope.py:81-82); v is copied
 // unchanged when requested (grad mode, rope.py:124-143).
 //
-// Layout: persistent CTAs, one per SM, of kHeadWarps warps; warp g of the grid
-// owns tokens g, g + W, ... and keeps a private ring of shared-memory stages.
-// Lane 0 streams each token's normed sections (q|k, contiguous in the qkv
-// row; with v the whole row) into a stage with one bulk copy (TMA engine)
-// completing on the stage's mbarrier.  A head spans L = hd/16 lanes; lane l
-// of a head holds dims [8l, 8l+8) of the first half and the same dims of the
-// second half, so the rotation pairs (i, i + hd/2) sit in one lane and the
-// canonical per-head sum (P = hd/8 partials) takes its first stride level in
-// the lane, then an xor butterfly over the L lanes.  32/L heads go per warp
-// iteration; each shared-memory read and global store covers whole 128-byte
-// lines of a head.
+// Layout: persistent CTAs, one per SM, of kHeadWarps warps.  The work unit
+// is one section of one token: its q or its k heads (normed, rotated), or its
+// v (copied, grad mode); unit u is section u % NU of token u / NU.  Warp w of
+// CTA c owns the units w*G + c + k*G*W (G CTAs of W warps: every SM gets the
+// same share), with a private ring of shared-memory stages (two measured best:
+// more stages delay each warp's first unit behind the others' copies).  Lane 0 streams
+// each unit into a stage with bulk copies (TMA engine) completing on the
+// stage's mbarrier: the section, and for a rotated section the token's cos and
+// sin rows, so no per-token global load sits on the critical path.  The norm
+// weights are bulk-copied into shared memory first, ahead of every unit.  A head spans
+// L = hd/16 lanes; lane l of a head holds dims [8l, 8l+8) of the first half
+// and the same dims of the second half, so the rotation pairs (i, i + hd/2)
+// sit in one lane and the canonical per-head sum (P = hd/8 partials) takes its
+// first stride level in the lane, then an xor butterfly over the L lanes.
+// 32/L heads go per warp iteration; each shared-memory read and global store
+// covers whole 128-byte lines of a head.
 #include "afb_device.cuh"
 #include "afb_launch.h"
 
@@ -47,7 +52,7 @@ struct HeadNormArgs {
 };
 
 constexpr int kHeadWarps = 16;
-constexpr int kHeadMaxStages = 4;
+constexpr int kHeadMaxStages = 2;
 constexpr int kHeadUnroll = 4;
 
 template <int HD, bool ROTATE, bool WITH_K, bool WITH_V>
@@ -56,7 +61,9 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
   constexpr int L = HD / 16;     // lanes per head
   constexpr int HPI = 32 / L;    // heads per warp iteration
   constexpr int HALF = HD / 2;
-  constexpr int NSEC = WITH_K ? 2 : 1;
+  constexpr int NSEC = WITH_K ? 2 : 1;               // normed sections per token
+  constexpr int NU = NSEC + (WITH_V ? 1 : 0);        // units per token
+  constexpr uint32_t kTabBytes = ROTATE ? 2u * HALF * 4u : 0u;
   extern __shared__ __align__(128) uint8_t smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -65,105 +72,132 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
   const int H = a.heads;
   const int iters = (H + HPI - 1) / HPI;
   const uint32_t sec_bytes = static_cast<uint32_t>(H) * HD * 2u;
-  // q (and k) are contiguous at the start of the row; with v the whole row.
-  const uint32_t stage_bytes = sec_bytes * (NSEC + (WITH_V ? 1u : 0u));
+  const uint32_t stage_bytes = sec_bytes + kTabBytes;
   uint8_t* ring = smem + static_cast<size_t>(warp) * nsw * stage_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kHeadWarps) * nsw * stage_bytes) +
-                   warp * nsw;
+  float* wsm = reinterpret_cast<float*>(smem + static_cast<size_t>(kHeadWarps) * nsw * stage_bytes);
+  uint64_t* bars0 = reinterpret_cast<uint64_t*>(wsm + NSEC * HD);
+  uint64_t* bars = bars0 + warp * nsw;
+  uint64_t* wbar = bars0 + kHeadWarps * nsw;
   if (lane == 0) {
     for (int s = 0; s < nsw; ++s) mbar_init(smem_addr(&bars[s]), 1);
+    if (warp == 0) mbar_init(smem_addr(wbar), 1);
     fence_mbar_init();
   }
-  __syncwarp();
+  __syncthreads();  // the weight barrier is waited on by every warp
   pdl_wait();
   pdl_trigger();
+  if (threadIdx.x == 0) {
+    // The norm weights go first, ahead of every unit.
+    mbar_arrive_expect_tx(smem_addr(wbar), NSEC * HD * 4u);
+    bulk_g2s(smem_addr(wsm), a.wq, HD * 4u, smem_addr(wbar));
+    if (WITH_K) bulk_g2s(smem_addr(wsm + HD), a.wk, HD * 4u, smem_addr(wbar));
+  }
+  __syncthreads();
 
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kHeadWarps + warp;
-  const int64_t nw = static_cast<int64_t>(gridDim.x) * kHeadWarps;
-  auto issue = [&](int64_t t) {  // lane 0: stream token gw + t*nw into stage t % nsw
-    const int64_t tok = gw + t * nw;
-    const int s = static_cast<int>(t % nsw);
+  const int64_t u1 = a.tokens * NU;  // units
+  auto unit_of = [&](int64_t j) {
+    return static_cast<int64_t>(warp) * gridDim.x + blockIdx.x + j * static_cast<int64_t>(gridDim.x) * kHeadWarps;
+  };
+  auto issue = [&](int64_t j) {  // lane 0: stream unit unit_of(j) into stage j % nsw
+    const int64_t u = unit_of(j);
+    const int64_t tok = u / NU;
+    const int sec = static_cast<int>(u % NU);
+    const int s = static_cast<int>(j % nsw);
+    uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
-    mbar_arrive_expect_tx(bar, stage_bytes);
-    bulk_g2s(smem_addr(ring + static_cast<size_t>(s) * stage_bytes), a.src + tok * a.src_row + a.q_off,
-             stage_bytes, bar);
+    const bool tab = ROTATE && sec < NSEC;
+    const int64_t off = sec == 0 ? a.q_off : (sec == 1 && WITH_K) ? a.k_off : a.v_off;
+    mbar_arrive_expect_tx(bar, sec_bytes + (tab ? kTabBytes : 0u));
+    bulk_g2s(smem_addr(st), a.src + tok * a.src_row + off, sec_bytes, bar);
+    if (tab) {
+      const int64_t pos = tok % a.seq;
+      bulk_g2s(smem_addr(st + sec_bytes), a.cos + pos * HALF, HALF * 4u, bar);
+      bulk_g2s(smem_addr(st + sec_bytes + HALF * 4u), a.sin + pos * HALF, HALF * 4u, bar);
+    }
   };
   if (lane == 0) {
-    for (int t = 0; t < nsw && gw + t * nw < a.tokens; ++t) issue(t);
+    for (int j = 0; j < nsw && unit_of(j) < u1; ++j) issue(j);
+  }
+  if (!mbar_wait(smem_addr(wbar), 0)) {
+    // Never expected: drain this warp's copies (bounded), then stop.
+    for (int64_t k = 0; k < nsw && unit_of(k) < u1; ++k)
+      mbar_wait(smem_addr(&bars[k % nsw]), 0);
+    if (threadIdx.x == 0) mbar_wait(smem_addr(wbar), 0);
+    return;
   }
 
-  for (int64_t t = 0; gw + t * nw < a.tokens; ++t) {
-    const int64_t tok = gw + t * nw;
-    const int s = static_cast<int>(t % nsw);
+  for (int64_t j = 0; unit_of(j) < u1; ++j) {
+    const int64_t u = unit_of(j);
+    const int64_t tok = u / NU;
+    const int sec = static_cast<int>(u % NU);
+    const int s = static_cast<int>(j % nsw);
     const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-    float cs[8], sn[8];
-    if (ROTATE) {  // issued before the wait: the tables do not depend on the stage
-      const int64_t pos = tok % a.seq;
-      const float* cp = a.cos + pos * HALF + 8 * l;
-      const float* sp = a.sin + pos * HALF + 8 * l;
-      const float4 c0 = ld_keep_f4(cp), c1 = ld_keep_f4(cp + 4);
-      const float4 s0 = ld_keep_f4(sp), s1 = ld_keep_f4(sp + 4);
-      cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
-      cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
-      sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-    }
-    if (!mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((t / nsw) & 1))) {
-      for (int64_t k = t + 1; k < t + nsw && gw + k * nw < a.tokens; ++k)
+    if (!mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
+      for (int64_t k = j + 1; k < j + nsw && unit_of(k) < u1; ++k)
         mbar_wait(smem_addr(&bars[k % nsw]), static_cast<uint32_t>((k / nsw) & 1));
       return;
     }
     const int64_t out_base = tok * static_cast<int64_t>(H) * HD;
-#pragma unroll
-    for (int sec = 0; sec < NSEC; ++sec) {
-      const uint8_t* in = st + sec * sec_bytes;
+    if (WITH_V && sec == NSEC) {
+      uint16_t* out = a.out_v + out_base;
+      const int nvec = H * HD / 8;
+      for (int v = lane; v < nvec; v += 32) st16(out + 8 * v, lds16(st + 16 * v));
+    } else {
       uint16_t* out = (sec ? a.out_k : a.out_q) + out_base;
-      float wa[8], wb[8];
+      float wa[8], wb[8], cs[8], sn[8];
       {
-        const float* wp = (sec ? a.wk : a.wq) + 8 * l;
-        const float4 w0 = ld_keep_f4(wp), w1 = ld_keep_f4(wp + 4);
-        const float4 w2 = ld_keep_f4(wp + HALF), w3 = ld_keep_f4(wp + HALF + 4);
+        const float4* wp = reinterpret_cast<const float4*>(wsm + sec * HD + 8 * l);
+        const float4 w0 = wp[0], w1 = wp[1], w2 = wp[HALF / 4], w3 = wp[HALF / 4 + 1];
         wa[0] = w0.x; wa[1] = w0.y; wa[2] = w0.z; wa[3] = w0.w;
         wa[4] = w1.x; wa[5] = w1.y; wa[6] = w1.z; wa[7] = w1.w;
         wb[0] = w2.x; wb[1] = w2.y; wb[2] = w2.z; wb[3] = w2.w;
         wb[4] = w3.x; wb[5] = w3.y; wb[6] = w3.z; wb[7] = w3.w;
       }
+      if (ROTATE) {
+        const float4* cp = reinterpret_cast<const float4*>(st + sec_bytes) + 2 * l;
+        const float4* sp = reinterpret_cast<const float4*>(st + sec_bytes + HALF * 4) + 2 * l;
+        const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+        cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+        cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+        sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+        sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+      }
       for (int it0 = 0; it0 < iters; it0 += kHeadUnroll) {
         uint4 va[kHeadUnroll], vb[kHeadUnroll];
         float ss[kHeadUnroll];
 #pragma unroll
-        for (int u = 0; u < kHeadUnroll; ++u) {
-          const int h = (it0 + u) * HPI + hsub;
-          const bool hv = it0 + u < iters && h < H;
-          va[u] = hv ? lds16(in + (h * HD + 8 * l) * 2) : make_uint4(0, 0, 0, 0);
-          vb[u] = hv ? lds16(in + (h * HD + HALF + 8 * l) * 2) : make_uint4(0, 0, 0, 0);
+        for (int uu = 0; uu < kHeadUnroll; ++uu) {
+          const int h = (it0 + uu) * HPI + hsub;
+          const bool hv = it0 + uu < iters && h < H;
+          va[uu] = hv ? lds16(st + (h * HD + 8 * l) * 2) : make_uint4(0, 0, 0, 0);
+          vb[uu] = hv ? lds16(st + (h * HD + HALF + 8 * l) * 2) : make_uint4(0, 0, 0, 0);
           float fa[8], fb[8];
-          unpack8(va[u], fa);
-          unpack8(vb[u], fb);
+          unpack8(va[uu], fa);
+          unpack8(vb[uu], fb);
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             fa[k] = __fmul_rn(fa[k], fa[k]);
             fb[k] = __fmul_rn(fb[k], fb[k]);
           }
-          ss[u] = __fadd_rn(vec_sum8(fa), vec_sum8(fb));  // partials v and v + L
+          ss[uu] = __fadd_rn(vec_sum8(fa), vec_sum8(fb));  // partials v and v + L
         }
 #pragma unroll
         for (int o = L / 2; o >= 1; o >>= 1) {
 #pragma unroll
-          for (int u = 0; u < kHeadUnroll; ++u) ss[u] = __fadd_rn(ss[u], __shfl_xor_sync(kFull, ss[u], o));
+          for (int uu = 0; uu < kHeadUnroll; ++uu) ss[uu] = __fadd_rn(ss[uu], __shfl_xor_sync(kFull, ss[uu], o));
         }
 #pragma unroll
-        for (int u = 0; u < kHeadUnroll; ++u) {
-          if (it0 + u >= iters) break;  // warp-uniform
-          const int h = (it0 + u) * HPI + hsub;
+        for (int uu = 0; uu < kHeadUnroll; ++uu) {
+          if (it0 + uu >= iters) break;  // warp-uniform
+          const int h = (it0 + uu) * HPI + hsub;
           // ss / HD with HD a power of two: the product by 1/HD rounds identically
-          const float rstd = canonical_rstd(__fmul_rn(ss[u], 1.0f / HD), a.eps);
+          const float rstd = canonical_rstd(__fmul_rn(ss[uu], 1.0f / HD), a.eps);
           const f2_t rr = f2(rstd, rstd);
           uint4 na, nb;  // bf16((x * rstd) * w), exact pairs of bf16
           {
             float fa[8], fb[8];
-            unpack8(va[u], fa);
-            unpack8(vb[u], fb);
+            unpack8(va[uu], fa);
+            unpack8(vb[uu], fb);
             uint32_t* pa = &na.x;
             uint32_t* pb = &nb.x;
 #pragma unroll
@@ -191,16 +225,10 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
         }
       }
     }
-    if (WITH_V) {
-      const uint8_t* in = st + NSEC * sec_bytes;
-      uint16_t* out = a.out_v + out_base;
-      const int nvec = H * HD / 8;
-      for (int v = lane; v < nvec; v += 32) st16(out + 8 * v, lds16(in + 16 * v));
-    }
     __syncwarp();
-    if (lane == 0 && gw + (t + nsw) * nw < a.tokens) {
+    if (lane == 0 && unit_of(j + nsw) < u1) {
       fence_proxy_async_smem();
-      issue(t + nsw);
+      issue(j + nsw);
     }
   }
 }
@@ -209,14 +237,15 @@ template <bool ROTATE, bool WITH_K, bool WITH_V>
 static cudaError_t launch_headnorm(const HeadNormArgs& a, int hd, cudaStream_t st) {
   const DeviceInfo& dev = device_info();
   if (dev.error != cudaSuccess) return dev.error;
-  const size_t stage = static_cast<size_t>(a.heads) * hd * 2 *
-                       ((WITH_K ? 2 : 1) + (WITH_V ? 1 : 0));
+  const size_t stage = static_cast<size_t>(a.heads) * hd * 2 + (ROTATE ? static_cast<size_t>(hd) * 4 : 0);
   const size_t per = kHeadWarps * (stage + sizeof(uint64_t));
-  int nsw = static_cast<int>(dev.max_smem_optin / per);
+  const size_t fixed = static_cast<size_t>(WITH_K ? 2 : 1) * hd * sizeof(float) + sizeof(uint64_t);
+  int nsw = static_cast<int>((dev.max_smem_optin - fixed) / per);
   if (nsw < 1) return cudaErrorInvalidValue;  // caller bounds heads * head_dim
   if (nsw > kHeadMaxStages) nsw = kHeadMaxStages;
-  const size_t smem = per * nsw;
-  const int64_t want = (a.tokens + kHeadWarps - 1) / kHeadWarps;
+  const size_t smem = fixed + per * nsw;
+  const int64_t units = a.tokens * ((WITH_K ? 2 : 1) + (WITH_V ? 1 : 0));
+  const int64_t want = (units + kHeadWarps - 1) / kHeadWarps;
   const dim3 grid(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
   const dim3 block(kHeadWarps * 32);
   auto go = [&](auto kern) -> cudaError_t {
