@@ -442,23 +442,25 @@ __device__ __forceinline__ float canonical_gelu(float x) {
 }
 
 // The same formula on the special-function unit (rcp.approx, ex2.approx).
-// Absolute error stays below 2^-20 + 2^-12 * |gelu(x)|; the row kernel uses it
-// for the codes and recomputes the canonical value for amax candidates.
+// It keeps the canonical formula's rounding structure where it matters: the
+// erfc term is subtracted from 1 with one rounding (y = RN(1 - p*e)) and
+// gelu = (x/2) * (1 +- y), so for x < 0, where 1 - y cancels, the fast value
+// sits on the same 2^-24 grid as the canonical one.  1/sqrt2 is folded into
+// the constants of t and of the exponent.  Absolute error stays below
+// 2^-20 + 2^-12 * |gelu(x)|; the row kernel uses it for the codes and
+// recomputes the canonical value for amax candidates.
 __device__ __forceinline__ float fast_gelu(float x) {
-  const float z = x * 0.707106769084930419921875f;
-  const float az = fabsf(z);
   float t;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(__fmaf_rn(0.3275911f, az, 1.0f)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(__fmaf_rn(fabsf(x), 0.3275911f * 0.707106769084930419921875f, 1.0f)));
   float p = __fmaf_rn(1.061405429f, t, -1.453152027f);
   p = __fmaf_rn(p, t, 1.421413741f);
   p = __fmaf_rn(p, t, -0.284496736f);
   p = __fmaf_rn(p, t, 0.254829592f);
   p = p * t;
   float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-(az * az) * 1.44269502162933349609375f));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"((x * x) * -0.721347520444481703680f));
   const float y = __fmaf_rn(-p, e, 1.0f);
-  const float erf = (z < 0.0f) ? -y : y;
-  return (0.5f * x) * (1.0f + erf);
+  return (0.5f * x) * (1.0f + copysignf(y, x));
 }
 
 }  // namespace afb

@@ -5,10 +5,13 @@
 //   y = gelu(x) if GELU else x                     (fp32)
 //   s = max(max|y|, 1e-12) / 448;  q = e4m3(clamp(y / s, +-448))
 //
-// Layout: a group of GROUP warps owns a row; thread t of the group holds the
-// 16-element chunks ch = t + 32*GROUP*c (c < CPL), i.e. two 16-byte loads and
-// one 16-byte FP8 store per chunk.  The amax is a max, so the order of the
-// reduction does not matter.
+// Layout: a group of GROUP warps owns a row (GROUP a power of two, 1..16,
+// chosen so that a thread holds at most two chunks); thread t of the group
+// holds the 16-element chunks ch = t + 32*GROUP*c (c < CPL), i.e. two 16-byte
+// loads and one 16-byte FP8 store per chunk.  A block is max(GROUP, 4) warps
+// (one or more rows).  The group's maxima are exchanged through shared memory
+// with one barrier each.  The amax is a max, so the order of the reduction
+// does not matter.
 //
 // Without GELU the codes and scales are exact: q = y / s is the product by
 // RN(1/s) where that provably gives the code of the IEEE quotient, and the
@@ -35,81 +38,86 @@ struct RowquantArgs {
   int K;
 };
 
+__host__ __device__ constexpr int rowquant_block_warps(int group) { return group > 4 ? group : 4; }
+
 template <int CPL, int GROUP, bool GELU>
-__global__ void __launch_bounds__(kRowWarps * 32)
+__global__ void __launch_bounds__(rowquant_block_warps(GROUP) * 32)
 rowquant_kernel(const RowquantArgs a) {
-  static_assert(kRowWarps % GROUP == 0, "GROUP must divide the CTA's warps");
-  __shared__ float red[kRowWarps];
+  constexpr int BW = rowquant_block_warps(GROUP);
+  __shared__ float red[2][BW];
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int t = (warp % GROUP) * 32 + lane;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowWarps / GROUP) + warp / GROUP;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (BW / GROUP) + warp / GROUP;
   const bool row_ok = row < a.rows;
   const int K = a.K;
   const int64_t base = (row_ok ? row : 0) * K;
 
-  uint4 xv[CPL][2];
-#pragma unroll
-  for (int c = 0; c < CPL; ++c) {
-    const int e = (t + 32 * GROUP * c) * 16;
-    const bool ok = row_ok && e < K;
-    xv[c][0] = ok ? ld_stream(a.x + base + e) : make_uint4(0, 0, 0, 0);
-    xv[c][1] = ok ? ld_stream(a.x + base + e + 8) : make_uint4(0, 0, 0, 0);
-  }
-
   float y[CPL][16];
   float amax = 0.0f;
+  {
+    uint4 xv[CPL][2];
 #pragma unroll
-  for (int c = 0; c < CPL; ++c) {
-    float lo[8], hi[8];
-    unpack8(xv[c][0], lo);
-    unpack8(xv[c][1], hi);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      y[c][k] = GELU ? fast_gelu(lo[k]) : lo[k];
-      y[c][k + 8] = GELU ? fast_gelu(hi[k]) : hi[k];
+    for (int c = 0; c < CPL; ++c) {
+      const int e = (t + 32 * GROUP * c) * 16;
+      const bool ok = row_ok && e < K;
+      xv[c][0] = ok ? ld_stream(a.x + base + e) : make_uint4(0, 0, 0, 0);
+      xv[c][1] = ok ? ld_stream(a.x + base + e + 8) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(y[c][k]));
+    for (int c = 0; c < CPL; ++c) {
+      float lo[8], hi[8];
+      unpack8(xv[c][0], lo);
+      unpack8(xv[c][1], hi);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        y[c][k] = GELU ? fast_gelu(lo[k]) : lo[k];
+        y[c][k + 8] = GELU ? fast_gelu(hi[k]) : hi[k];
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(y[c][k]));
+    }
   }
   const float lamax = amax;
 
-  // Group-wide max.  Padding elements are zero and leave the max unchanged.
-  auto group_max = [&](float v) {
+  // Group-wide max through red[buf].  Padding elements are zero and leave the
+  // max unchanged.  The two exchanges of a row use different buffers.
+  auto group_max = [&](float v, int buf) {
     v = warp_max(v);
     if (GROUP > 1) {
-      __syncthreads();
-      if (lane == 0) red[warp] = v;
+      if (lane == 0) red[buf][warp] = v;
       __syncthreads();
       const int w0 = (warp / GROUP) * GROUP;
 #pragma unroll
-      for (int w = 0; w < GROUP; ++w) v = fmaxf(v, red[w0 + w]);
+      for (int w = 0; w < GROUP; ++w) v = fmaxf(v, red[buf][w0 + w]);
     }
     return v;
   };
-  amax = group_max(amax);
+  amax = group_max(amax, 0);
 
   if (GELU) {
     // Exact amax over the candidates (see the file comment).  A thread whose
-    // own fast maximum is below the threshold holds no candidate.
+    // own fast maximum is below the threshold holds no candidate; the rare
+    // candidates re-read their input element.
     const float margin = __fmaf_rn(amax, 0x1p-11f, 0x1p-19f);
     const float thresh = amax - margin;
     float exact = 0.0f;
     if (lamax >= thresh) {
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {
+        const int e = (t + 32 * GROUP * c) * 16;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           if (fabsf(y[c][k]) >= thresh) {
-            const float xk = unpack_at(xv[c][k >> 3], k & 7);
+            const float xk = __uint_as_float(static_cast<uint32_t>(__ldg(a.x + base + e + k)) << 16);
             exact = fmaxf(exact, fabsf(canonical_gelu_call(xk)));
           }
         }
       }
     }
-    amax = group_max(exact);
+    amax = group_max(exact, 1);
   }
 
   const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
@@ -144,40 +152,38 @@ rowquant_kernel(const RowquantArgs a) {
   if (t == 0) a.s[row] = s;
 }
 
-// Threads-per-row grouping and chunks per thread for a row of K elements.
+// Threads-per-row grouping and chunks per thread for a row of K elements:
+// the smallest power-of-two group whose threads hold at most two chunks each.
 static bool rowquant_shape(int64_t K, int* group, int* cpl) {
   const int64_t chunks = (K + 15) / 16;
-  if (chunks <= 32 * 4) {
-    *group = 1;
-    *cpl = chunks <= 32 ? 1 : chunks <= 64 ? 2 : 4;
-    return true;
-  }
-  if (chunks <= 128 * 8) {
-    *group = 4;
-    *cpl = chunks <= 128 * 2 ? 2 : chunks <= 128 * 4 ? 4 : 8;
-    return true;
-  }
-  return false;
+  int g = 1;
+  while (g < 16 && chunks > 64 * g) g <<= 1;
+  if (chunks > 64 * g) return false;
+  *group = g;
+  *cpl = chunks > 32 * g ? 2 : 1;
+  return true;
+}
+
+template <int GROUP, bool GELU>
+static cudaError_t launch_rowquant_g(const RowquantArgs& a, int cpl, cudaStream_t st) {
+  constexpr int BW = rowquant_block_warps(GROUP);
+  const int rows_per_block = BW / GROUP;
+  const dim3 grid(static_cast<unsigned>((a.rows + rows_per_block - 1) / rows_per_block));
+  const dim3 block(BW * 32);
+  return cpl == 1 ? launch_pdl(rowquant_kernel<1, GROUP, GELU>, grid, block, 0, st, a)
+                  : launch_pdl(rowquant_kernel<2, GROUP, GELU>, grid, block, 0, st, a);
 }
 
 template <bool GELU>
 static cudaError_t launch_rowquant(const RowquantArgs& a, cudaStream_t st) {
   int group = 0, cpl = 0;
   if (!rowquant_shape(a.K, &group, &cpl)) return cudaErrorInvalidValue;
-  const int rows_per_cta = kRowWarps / group;
-  const dim3 grid(static_cast<unsigned>((a.rows + rows_per_cta - 1) / rows_per_cta));
-  const dim3 block(kRowWarps * 32);
-  if (group == 1) {
-    switch (cpl) {
-      case 1: return launch_pdl(rowquant_kernel<1, 1, GELU>, grid, block, 0, st, a);
-      case 2: return launch_pdl(rowquant_kernel<2, 1, GELU>, grid, block, 0, st, a);
-      default: return launch_pdl(rowquant_kernel<4, 1, GELU>, grid, block, 0, st, a);
-    }
-  }
-  switch (cpl) {
-    case 2: return launch_pdl(rowquant_kernel<2, 4, GELU>, grid, block, 0, st, a);
-    case 4: return launch_pdl(rowquant_kernel<4, 4, GELU>, grid, block, 0, st, a);
-    default: return launch_pdl(rowquant_kernel<8, 4, GELU>, grid, block, 0, st, a);
+  switch (group) {
+    case 1: return launch_rowquant_g<1, GELU>(a, cpl, st);
+    case 2: return launch_rowquant_g<2, GELU>(a, cpl, st);
+    case 4: return launch_rowquant_g<4, GELU>(a, cpl, st);
+    case 8: return launch_rowquant_g<8, GELU>(a, cpl, st);
+    default: return launch_rowquant_g<16, GELU>(a, cpl, st);
   }
 }
 
