@@ -110,7 +110,11 @@ __device__ __forceinline__ float round_bf(float x) {
 // ---------------------------------------------------------------------------
 // FP8 e4m3 (OCP "fn" variant, max 448): RNE with saturation to +-448.
 // cvt.rn.satfinite.e4m3x2.f32 d, a, b puts a in the high byte, b in the low.
+// The reference clamps to [-448, 448] before converting; satfinite already
+// saturates every finite value and infinity, so clamp448 only has to map NaN
+// to -448 as the clamp's max(NaN, -448) does.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ float clamp448(float v) { return fmaxf(v, -448.0f); }
 __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   unsigned short r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
@@ -152,7 +156,7 @@ __device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, float 
     for (int k = 0; k < 8; ++k) q[k] = __fdiv_rn(y[k], s);
   }
 #pragma unroll
-  for (int k = 0; k < 8; ++k) q[k] = fminf(fmaxf(q[k], -448.0f), 448.0f);
+  for (int k = 0; k < 8; ++k) q[k] = clamp448(q[k]);
   return e4m3x8(q);
 }
 
@@ -460,7 +464,9 @@ __device__ __forceinline__ float fast_gelu(float x) {
   float e;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"((x * x) * -0.721347520444481703680f));
   const float y = __fmaf_rn(-p, e, 1.0f);
-  return (0.5f * x) * (1.0f + copysignf(y, x));
+  // (x/2) * (1 +- y) == x * (1/2 +- y/2): halving is exact, so one FMA forms
+  // the same rounded factor.
+  return x * __fmaf_rn(0.5f, copysignf(y, x), 0.5f);
 }
 
 }  // namespace afb

@@ -137,8 +137,8 @@ rowquant_kernel(const RowquantArgs a) {
       if (GELU) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          lo[k] = fminf(fmaxf(__fmul_rn(lo[k], r), -448.0f), 448.0f);
-          hi[k] = fminf(fmaxf(__fmul_rn(hi[k], r), -448.0f), 448.0f);
+          lo[k] = clamp448(__fmul_rn(lo[k], r));
+          hi[k] = clamp448(__fmul_rn(hi[k], r));
         }
         plo = e4m3x8(lo);
         phi = e4m3x8(hi);

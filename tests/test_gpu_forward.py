@@ -143,6 +143,43 @@ def test_rowquant_codes_at_e4m3_midpoints(K, cuda_dev):
     np.testing.assert_array_equal(to_bits(q), oq)
 
 
+def _nonfinite_rows(K: int) -> np.ndarray:
+    r = rng(K + 99)
+    x = r.standard_normal((5, K)).astype(np.float32)
+    x[0, 5], x[0, 100] = np.nan, -0.0
+    x[1, 7] = np.inf
+    x[2, :] = 0.0
+    x[2, 3] = -0.0
+    x[3, 9], x[3, 10] = -np.inf, np.nan
+    x[4, 11] = np.nan
+    return bf_bits(x[None])
+
+
+@pytest.mark.parametrize("K", [2048, 8192])
+def test_rowquant_nonfinite_and_signed_zero(K, cuda_dev):
+    """NaN takes the code of -448 (the reference clamps with max(NaN, -448)),
+    an infinite row max gives an infinite scale, an all-zero row the 1e-12
+    floor, and zeros keep their sign: bit-exact against the oracle."""
+    x = _nonfinite_rows(K)
+    q, s = afb.rowquant(dev(x, cuda_dev), gelu=False)
+    oq, os_ = C.rowquant(x)
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), os_.view(np.uint32))
+    np.testing.assert_array_equal(to_bits(q), oq)
+
+
+def test_rowquant_gelu_nan_codes(cuda_dev):
+    """GELU path: NaN inputs leave the exact scale alone and take code -448."""
+    K = 8192
+    x = _nonfinite_rows(K)[:, [0, 2, 4]]
+    q, s = afb.rowquant(dev(x, cuda_dev), gelu=True)
+    oq, os_ = C.rowquant(x, gelu=True)
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), os_.view(np.uint32))
+    xf = from_bits(x, "cpu").float().numpy().reshape(3, K)
+    qb = to_bits(q).reshape(3, K)
+    nan = np.isnan(xf)
+    assert nan.sum() == 2 and np.all(qb[nan] == 0xFE) and np.all(oq.reshape(3, K)[nan] == 0xFE)
+
+
 def _codes_at_ties_only(q_bits, y, s):
     """Codes equal e4m3(y/s) except where y/s is within 4 fp32 ulp of an e4m3 tie."""
     rows = s.shape[0]
