@@ -12,11 +12,23 @@
 //   dshift[b] += gh;  dscale[b] += gh * xhat;  dgate[b] += dz * x   (fp32)
 //
 // Parameter-gradient order (deterministic, independent of the launch shape):
-// the rows of each batch entry are cut into chunks of kChunkRows; in a chunk,
-// warp w sums rows w, w + 4, w + 8, ... in increasing order; the four warp
-// sums combine as a stride tree, (p0 + p2) + (p1 + p3); the chunk sums combine
-// by a stride tree over the chunk index (finalize.cu) and round to bf16.  The chunk sums live in
-// a caller-provided fp32 workspace [B][chunks][NQ][D].
+// the rows of each batch entry are cut into chunks of kChunkRows = 16; in a
+// chunk, stream w (w < 4) sums rows w, w + 4, w + 8, w + 12 in increasing
+// order from zero; the four stream sums combine as a stride tree,
+// (p0 + p2) + (p1 + p3); the chunk sums combine by a stride tree over the
+// chunk index (finalize.cu) and round to bf16.
+//
+// Two passes, so that no thread needs a whole row's parameter sums:
+//  1. adaln_bwd_stats_kernel, one row per warp pair as in the forward kernel
+//     (bulk-copied z and gh, scale rows in shared memory): the row scalars
+//     mean, rstd, c1, c2 (canonical sums) into the workspace.
+//  2. adaln_bwd_cols_kernel, one 8-column vector per thread and one chunk per
+//     CTA: the thread walks the chunk's rows in stream order, forms dz and dx
+//     from the row scalars, stores them, and keeps its columns' stream sums in
+//     registers.  z and gh were just read by pass 1 and are normally still in
+//     the L2, so the DRAM traffic stays close to one pass.
+// Workspace: [rows][4] fp32 row scalars, then the [B][chunks][NQ][D] fp32
+// chunk sums.
 #include <map>
 #include <mutex>
 
@@ -25,198 +37,325 @@
 
 namespace afb {
 
-constexpr int kBwdWarps = 4;
-constexpr int kRowsPerWarp = 4;
-constexpr int kChunkRows = kBwdWarps * kRowsPerWarp;
+constexpr int kStreams = 4;
+constexpr int kRowsPerStream = 4;
+constexpr int kChunkRows = kStreams * kRowsPerStream;
 
-struct AdalnBwdArgs {
+// ---------------------------------------------------------------------------
+// Pass 1: row scalars.
+// ---------------------------------------------------------------------------
+constexpr int kStatPairs = 8;
+constexpr int kStatWarps = 2 * kStatPairs;
+constexpr int kStatStages = 2;
+constexpr int kStatModSlots = 2;
+// Per pair: exchange buffers A (mean), B (variance) of 2 warps x 4 pairs x 32
+// lanes, and C (c1 and c2 together) of twice that.
+constexpr size_t kStatXchF2 = 4 * 2 * 4 * 32;
+
+struct AdalnStatsArgs {
+  const uint16_t* gh;     // [rows, D]
+  const uint16_t* z;      // [rows, D]
+  const uint16_t* scale;  // [B, D]
+  float4* stats;          // [rows] (mean, rstd, c1, c2)
+  int64_t rows;
+  int64_t seq;
+  int dim;
+  float eps;
+};
+
+template <int NC, bool EXACT>
+__global__ void __launch_bounds__(kStatWarps * 32, 1)
+adaln_bwd_stats_kernel(const AdalnStatsArgs a, const int use_smods) {
+  constexpr bool SPLIT = NC >= 2;
+  constexpr int NH = SPLIT ? NC / 2 : 1;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int pair = warp >> 1;
+  const int h = warp & 1;
+  const int bar_id = 1 + pair;
+  const bool leader = h == 0 && lane == 0;
+  const int D = EXACT ? NC * 256 : a.dim;
+  const uint32_t row_bytes = static_cast<uint32_t>(D) * 2u;
+  const uint32_t stage_bytes = 2u * row_bytes;  // z | gh
+  const size_t ring_all = static_cast<size_t>(kStatPairs) * kStatStages * stage_bytes;
+  uint8_t* ring = smem + static_cast<size_t>(pair) * kStatStages * stage_bytes;
+  f2_t* xch = reinterpret_cast<f2_t*>(smem + ring_all) + pair * kStatXchF2;
+  uint8_t* mods = smem + ring_all + kStatPairs * kStatXchF2 * sizeof(f2_t);
+  uint64_t* bars0 = reinterpret_cast<uint64_t*>(mods + (use_smods ? kStatModSlots * row_bytes : 0u));
+  uint64_t* bars = bars0 + pair * kStatStages;
+  uint64_t* modbar = bars0 + kStatPairs * kStatStages;
+
+  const int64_t r0 = a.rows * blockIdx.x / gridDim.x;
+  const int64_t r1 = a.rows * (blockIdx.x + 1) / gridDim.x;
+  const int64_t b_lo = r1 > r0 ? r0 / a.seq : 0;
+  const int64_t b_hi = r1 > r0 ? (r1 - 1) / a.seq : 0;
+  const bool smods = use_smods && r1 > r0 && b_hi - b_lo < kStatModSlots;
+  if (leader) {
+    for (int s = 0; s < kStatStages; ++s) mbar_init(smem_addr(&bars[s]), 1);
+    if (pair == 0) mbar_init(smem_addr(modbar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (smods && threadIdx.x == 0) {  // the scale rows go first, ahead of every row stage
+    const int nb = static_cast<int>(b_hi - b_lo + 1);
+    mbar_arrive_expect_tx(smem_addr(modbar), static_cast<uint32_t>(nb) * row_bytes);
+    for (int k = 0; k < nb; ++k)
+      bulk_g2s(smem_addr(mods + k * row_bytes), a.scale + (b_lo + k) * D, row_bytes, smem_addr(modbar));
+  }
+  if (smods) __syncthreads();
+
+  auto row_of = [&](int64_t j) { return r0 + pair + j * kStatPairs; };
+  auto issue = [&](int64_t j) {
+    const int64_t row = row_of(j);
+    const int s = static_cast<int>(j % kStatStages);
+    uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
+    const uint32_t bar = smem_addr(&bars[s]);
+    mbar_arrive_expect_tx(bar, stage_bytes);
+    bulk_g2s(smem_addr(st), a.z + row * D, row_bytes, bar);
+    bulk_g2s(smem_addr(st + row_bytes), a.gh + row * D, row_bytes, bar);
+  };
+  if (leader) {
+    for (int j = 0; j < kStatStages && row_of(j) < r1; ++j) issue(j);
+  }
+  auto col = [&](int i) { return (lane + 32 * (SPLIT ? 2 * i + h : i)) * 8; };
+  auto ok = [&](int i) { return EXACT || col(i) < D; };
+  auto div_d = [&](float x) {
+    return EXACT ? __fmul_rn(x, 1.0f / (NC * 256)) : __fdiv_rn(x, static_cast<float>(D));
+  };
+
+  bool dead = false;
+  int64_t jdead = 0;
+  if (smods && !mbar_wait(smem_addr(modbar), 0)) dead = true;
+  for (int64_t j = 0; row_of(j) < r1; ++j) {
+    const int64_t row = row_of(j);
+    const int s = static_cast<int>(j % kStatStages);
+    const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
+    if (!dead && !mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / kStatStages) & 1))) {
+      dead = true;
+      jdead = j;
+    }
+    const int64_t b = row / a.seq;
+    f2_t zf[NH][4];
+    uint4 gv[NH];
+#pragma unroll
+    for (int i = 0; i < NH; ++i) {
+      const uint4 zv = ok(i) ? lds16(st + col(i) * 2) : make_uint4(0, 0, 0, 0);
+      gv[i] = ok(i) ? lds16(st + row_bytes + col(i) * 2) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) zf[i][jj] = bf2f2(word(zv, jj));
+    }
+    const float mean = div_d(pair_canonical_sum2<NH, SPLIT>([&](int i, int jj) { return zf[i][jj]; }, xch,
+                                                             h, lane, bar_id));
+    if (!SPLIT) named_bar_sync(bar_id, 64);
+    if (leader && !dead && row_of(j + kStatStages) < r1) {  // both warps have read the stage
+      fence_proxy_async_smem();
+      issue(j + kStatStages);
+    }
+    const f2_t mm = f2(mean, mean);
+#pragma unroll
+    for (int i = 0; i < NH; ++i) {
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) zf[i][jj] = ok(i) ? sub2(zf[i][jj], mm) : 0ull;  // d = z - mean
+    }
+    const float rstd = canonical_rstd(
+        div_d(pair_canonical_sum2<NH, SPLIT>([&](int i, int jj) { return mul2_noc(zf[i][jj], zf[i][jj]); },
+                                            xch + 2 * 4 * 32, h, lane, bar_id)),
+        a.eps);
+    const f2_t rr = f2(rstd, rstd);
+    // dxh = gh * scale (kept in gv's place as fp32 pairs); xhat = d * rstd
+    f2_t dxh[NH][4];
+#pragma unroll
+    for (int i = 0; i < NH; ++i) {
+      const uint4 scv = !ok(i) ? make_uint4(0, 0, 0, 0)
+                        : smods ? lds16(mods + static_cast<size_t>(b - b_lo) * row_bytes + col(i) * 2)
+                                : ld_keep(a.scale + b * D + col(i));
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) dxh[i][jj] = mul2_noc(bf2f2(word(gv[i], jj)), bf2f2(word(scv, jj)));
+    }
+    float c1, c2;
+    pair_canonical_sum2x2<NH, SPLIT>(
+        [&](int n, int i, int jj) { return n == 0 ? dxh[i][jj] : mul2_noc(dxh[i][jj], mul2(zf[i][jj], rr)); },
+        xch + 2 * 2 * 4 * 32, h, lane, bar_id, c1, c2);
+    c1 = div_d(c1);
+    c2 = div_d(c2);
+    if (leader && !dead) a.stats[row] = make_float4(mean, rstd, c1, c2);
+  }
+  if (leader && dead) {
+    for (int64_t k = jdead; k < jdead + kStatStages && row_of(k) < r1; ++k)
+      mbar_wait(smem_addr(&bars[k % kStatStages]), static_cast<uint32_t>((k / kStatStages) & 1));
+    if (pair == 0 && smods) mbar_wait(smem_addr(modbar), 0);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pass 2: dz, dx and the chunk sums of the parameter gradients.  Lane group w
+// (lanes 8w .. 8w+7) of a warp runs stream w of one chunk for 8 consecutive
+// 8-column vectors: its four rows are loaded at once, so a thread makes one
+// round trip.  The stream sums combine by xor shuffles in the canonical order:
+// (p0 + p2) and (p1 + p3) across lane distance 16, then their sum across 8.
+// ---------------------------------------------------------------------------
+constexpr int kColWarps = 4;
+constexpr int kColVecsPerWarp = 8;                                   // 64 columns per warp
+constexpr int kColCols = kColWarps * kColVecsPerWarp * 8;             // 256 columns per CTA
+
+struct AdalnColsArgs {
   const uint16_t* gh;     // [rows, D]
   const uint16_t* gz;     // [rows, D] or null
   const uint16_t* z;      // [rows, D]
   const uint16_t* x;      // [rows, D] (HAS_X)
   const uint16_t* gate;   // [B, D] (HAS_X)
   const uint16_t* scale;  // [B, D]
+  const float4* stats;    // [rows]
   uint16_t* dz;           // [rows, D]
   uint16_t* dx;           // [rows, D] (HAS_X)
   float* part;            // [B][chunks][NQ][D]
   int64_t seq;
-  int64_t chunks;         // per batch entry
+  int64_t chunks;
   int dim;
-  float eps;
 };
 
-// Shared-memory words per warp: NQ accumulators per column.
 template <bool HAS_X>
 __host__ __device__ constexpr int bwd_nq() { return HAS_X ? 3 : 2; }
 
-template <int NC, bool HAS_X, bool HAS_GZ>
-__global__ void __launch_bounds__(kBwdWarps * 32)
-adaln_bwd_kernel(const AdalnBwdArgs a) {
+// grid (ceil(D / 256), chunks, B)
+template <bool HAS_X, bool HAS_GZ>
+__global__ void __launch_bounds__(kColWarps * 32, 4)
+adaln_bwd_cols_kernel(const AdalnColsArgs a) {
   constexpr int NQ = bwd_nq<HAS_X>();
-  extern __shared__ float4 smem4[];
-  float* acc_all = reinterpret_cast<float*>(smem4);
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  const int w = lane >> 3;  // stream
+  const int64_t ch = blockIdx.y;
+  const int64_t b = blockIdx.z;
   const int D = a.dim;
-  const int64_t b = blockIdx.y;
-  const int64_t chunk = blockIdx.x;
-  const int64_t pbase = b * D;
-  // Per-warp accumulators, NQ planes of NC*256 floats laid out [c][half][lane][4]
-  // so that every warp-wide float4 access is 512 contiguous bytes.
-  constexpr int kPlane = NC * 256;
-  float* acc = acc_all + static_cast<int64_t>(warp) * NQ * kPlane;
-  auto slot = [&](int q, int c, int half) {
-    return reinterpret_cast<float4*>(acc + q * kPlane + ((c * 2 + half) * 32 + lane) * 4);
-  };
-  const float fd = static_cast<float>(D);
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-#pragma unroll
-    for (int q = 0; q < NQ; ++q) {
-      *slot(q, c, 0) = make_float4(0.f, 0.f, 0.f, 0.f);
-      *slot(q, c, 1) = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  }
+  const int col = ((blockIdx.x * kColWarps + warp) * kColVecsPerWarp + (lane & 7)) * 8;
+  const bool cok = col < D;
+  const int64_t s0 = ch * kChunkRows;
 
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int64_t s = chunk * kChunkRows + i * kBwdWarps + warp;
-    if (s >= a.seq) break;  // warp-uniform
-    const int64_t base = (b * a.seq + s) * D;
-    uint4 zv[NC], gv[NC];
+  float acc[NQ][8];
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      const int e = (lane + 32 * c) * 8;
-      const bool ok = e < D;
-      zv[c] = ok ? ld_stream(a.z + base + e) : make_uint4(0, 0, 0, 0);
-      gv[c] = ok ? ld_stream(a.gh + base + e) : make_uint4(0, 0, 0, 0);
+  for (int q = 0; q < NQ; ++q)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[q][k] = 0.0f;
+  if (cok) {
+    uint4 zv[kRowsPerStream], gv[kRowsPerStream], gzv[kRowsPerStream], xv[kRowsPerStream];
+    float4 t[kRowsPerStream];
+#pragma unroll
+    for (int r = 0; r < kRowsPerStream; ++r) {  // the stream's rows, all in flight at once
+      const int64_t s = s0 + r * kStreams + w;
+      if (s < a.seq) {
+        const int64_t o = (b * a.seq + s) * D + col;
+        zv[r] = ld_stream(a.z + o);
+        gv[r] = ld_stream(a.gh + o);
+        if (HAS_GZ) gzv[r] = ld_stream(a.gz + o);
+        if (HAS_X) xv[r] = ld_stream(a.x + o);
+        t[r] = a.stats[b * a.seq + s];  // mean, rstd, c1, c2
+      }
     }
-    // statistics of z, exactly as the forward
-    const float mean = __fdiv_rn(
-        warp_canonical_sum_fn<NC>([&](int c, int k) { return unpack_at(zv[c], k); }), fd);
-    const float rstd = canonical_rstd(
-        __fdiv_rn(warp_canonical_sum_fn<NC>([&](int c, int k) {
-                    const float d = ((lane + 32 * c) * 8 < D) ? __fsub_rn(unpack_at(zv[c], k), mean)
-                                                              : 0.0f;
-                    return __fmul_rn(d, d);
-                  }),
-                  fd),
-        a.eps);
-    // c1 = sum(dxh) / D, c2 = sum(dxh * xhat) / D
-    uint4 scv[NC];
+    float sc[8], gt[8];
+    unpack8(ld_keep(a.scale + b * D + col), sc);
+    if (HAS_X) unpack8(ld_keep(a.gate + b * D + col), gt);
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      const int e = (lane + 32 * c) * 8;
-      scv[c] = (e < D) ? ld_keep(a.scale + pbase + e) : make_uint4(0, 0, 0, 0);
-    }
-    const float c1 = __fdiv_rn(warp_canonical_sum_fn<NC>([&](int c, int k) {
-                                 return __fmul_rn(unpack_at(gv[c], k), unpack_at(scv[c], k));
-                               }),
-                               fd);
-    const float c2 = __fdiv_rn(warp_canonical_sum_fn<NC>([&](int c, int k) {
-                                 if ((lane + 32 * c) * 8 >= D) return 0.0f;
-                                 const float xhat =
-                                     __fmul_rn(__fsub_rn(unpack_at(zv[c], k), mean), rstd);
-                                 const float dxh = __fmul_rn(unpack_at(gv[c], k), unpack_at(scv[c], k));
-                                 return __fmul_rn(dxh, xhat);
-                               }),
-                               fd);
-    // dz, dx and the column accumulators
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      const int e = (lane + 32 * c) * 8;
-      if (e >= D) continue;
-      float sc[8], g8[8], gz8[8], x8[8], dzf[8];
-      unpack8(scv[c], sc);
-      if (HAS_GZ) unpack8(ld_stream(a.gz + base + e), gz8);
-      if (HAS_X) {
-        unpack8(ld_keep(a.gate + pbase + e), g8);
-        unpack8(ld_stream(a.x + base + e), x8);
-      }
-      float sh_acc[8], sc_acc[8], g_acc[8];
-      {
-        const float4 p0 = *slot(0, c, 0), p1 = *slot(0, c, 1), q0 = *slot(1, c, 0), q1 = *slot(1, c, 1);
-        sh_acc[0] = p0.x; sh_acc[1] = p0.y; sh_acc[2] = p0.z; sh_acc[3] = p0.w;
-        sh_acc[4] = p1.x; sh_acc[5] = p1.y; sh_acc[6] = p1.z; sh_acc[7] = p1.w;
-        sc_acc[0] = q0.x; sc_acc[1] = q0.y; sc_acc[2] = q0.z; sc_acc[3] = q0.w;
-        sc_acc[4] = q1.x; sc_acc[5] = q1.y; sc_acc[6] = q1.z; sc_acc[7] = q1.w;
-      }
-      if (HAS_X) {
-        const float4 r0 = *slot(2, c, 0), r1 = *slot(2, c, 1);
-        g_acc[0] = r0.x; g_acc[1] = r0.y; g_acc[2] = r0.z; g_acc[3] = r0.w;
-        g_acc[4] = r1.x; g_acc[5] = r1.y; g_acc[6] = r1.z; g_acc[7] = r1.w;
-      }
-      float dxf[8];
+    for (int r = 0; r < kRowsPerStream; ++r) {
+      const int64_t s = s0 + r * kStreams + w;
+      if (s >= a.seq) break;
+      const int64_t o = (b * a.seq + s) * D + col;
+      float dzf[8], dxf[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float gh = unpack_at(gv[c], k);
-        const float xhat = __fmul_rn(__fsub_rn(unpack_at(zv[c], k), mean), rstd);
-        const float dxh = __fmul_rn(gh, sc[k]);
-        float dz = __fmul_rn(rstd, __fsub_rn(__fsub_rn(dxh, c1), __fmul_rn(xhat, c2)));
-        if (HAS_GZ) dz = __fadd_rn(dz, gz8[k]);
+        const float g = unpack_at(gv[r], k);
+        const float xhat = __fmul_rn(__fsub_rn(unpack_at(zv[r], k), t[r].x), t[r].y);
+        const float dxh = __fmul_rn(g, sc[k]);
+        float dz = __fmul_rn(t[r].y, __fsub_rn(__fsub_rn(dxh, t[r].z), __fmul_rn(xhat, t[r].w)));
+        if (HAS_GZ) dz = __fadd_rn(dz, unpack_at(gzv[r], k));
         dzf[k] = dz;
-        sh_acc[k] = __fadd_rn(sh_acc[k], gh);
-        sc_acc[k] = __fadd_rn(sc_acc[k], __fmul_rn(gh, xhat));
+        acc[0][k] = __fadd_rn(acc[0][k], g);
+        acc[1][k] = __fadd_rn(acc[1][k], __fmul_rn(g, xhat));
         if (HAS_X) {
-          dxf[k] = __fmul_rn(dz, g8[k]);
-          g_acc[k] = __fadd_rn(g_acc[k], __fmul_rn(dz, x8[k]));
+          dxf[k] = __fmul_rn(dz, gt[k]);
+          acc[2][k] = __fadd_rn(acc[2][k], __fmul_rn(dz, unpack_at(xv[r], k)));
         }
       }
-      st16(a.dz + base + e, pack8_rn(dzf));
-      if (HAS_X) st16(a.dx + base + e, pack8_rn(dxf));
-      *slot(0, c, 0) = make_float4(sh_acc[0], sh_acc[1], sh_acc[2], sh_acc[3]);
-      *slot(0, c, 1) = make_float4(sh_acc[4], sh_acc[5], sh_acc[6], sh_acc[7]);
-      *slot(1, c, 0) = make_float4(sc_acc[0], sc_acc[1], sc_acc[2], sc_acc[3]);
-      *slot(1, c, 1) = make_float4(sc_acc[4], sc_acc[5], sc_acc[6], sc_acc[7]);
-      if (HAS_X) {
-        *slot(2, c, 0) = make_float4(g_acc[0], g_acc[1], g_acc[2], g_acc[3]);
-        *slot(2, c, 1) = make_float4(g_acc[4], g_acc[5], g_acc[6], g_acc[7]);
-      }
+      st16(a.dz + o, pack8_rn(dzf));
+      if (HAS_X) st16(a.dx + o, pack8_rn(dxf));
     }
   }
-
-  // Chunk partial: stride tree over the warps, (p0 + p2) + (p1 + p3).
-  __syncthreads();
-  float* out = a.part + ((b * a.chunks + chunk) * NQ) * D;
-  const int stride = NQ * kPlane;
-  for (int i = threadIdx.x; i < NQ * kPlane; i += blockDim.x) {
-    const int q = i / kPlane, r = i % kPlane;
-    const int kk = r & 3, ln = (r >> 2) & 31, half = (r >> 7) & 1, c = r >> 8;
-    const int col = (ln + 32 * c) * 8 + half * 4 + kk;
-    if (col >= D) continue;
-    const float p0 = acc_all[i], p1 = acc_all[stride + i];
-    const float p2 = acc_all[2 * stride + i], p3 = acc_all[3 * stride + i];
-    out[q * D + col] = __fadd_rn(__fadd_rn(p0, p2), __fadd_rn(p1, p3));
+  // (p0 + p2) + (p1 + p3): lane groups 0/2 and 1/3 are 16 lanes apart, then
+  // groups 0/1 are 8 apart.  Commutative adds give the same bits in every lane.
+#pragma unroll
+  for (int q = 0; q < NQ; ++q)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float v = __fadd_rn(acc[q][k], __shfl_xor_sync(kFull, acc[q][k], 16));
+      acc[q][k] = __fadd_rn(v, __shfl_xor_sync(kFull, v, 8));
+    }
+  if (cok && w == 0) {
+    float* out = a.part + ((b * a.chunks + ch) * NQ) * D + col;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      float4* o4 = reinterpret_cast<float4*>(out + q * D);
+      o4[0] = make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
+      o4[1] = make_float4(acc[q][4], acc[q][5], acc[q][6], acc[q][7]);
+    }
   }
 }
 
-template <bool HAS_X, bool HAS_GZ>
-static cudaError_t launch_adaln_bwd(const AdalnBwdArgs& a, int64_t batch, cudaStream_t st) {
-  constexpr int NQ = bwd_nq<HAS_X>();
-  const size_t smem = static_cast<size_t>(kBwdWarps) * NQ * row_chunks(a.dim) * 256 * sizeof(float);
-  const dim3 grid(static_cast<unsigned>(a.chunks), static_cast<unsigned>(batch));
-  const dim3 block(kBwdWarps * 32);
-  cudaError_t e = cudaErrorInvalidValue;
-  auto go = [&](auto kern) {
-    cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (r != cudaSuccess) return r;
-    return launch_pdl(kern, grid, block, smem, st, a);
+// Pass-1 launch plan: shared memory for the rings, exchange buffers, and (when
+// they fit) the scale slots.
+static cudaError_t launch_adaln_bwd_stats(const AdalnStatsArgs& a, cudaStream_t st) {
+  const DeviceInfo& dev = device_info();
+  if (dev.error != cudaSuccess) return dev.error;
+  const size_t row = static_cast<size_t>(a.dim) * 2;
+  const size_t base = static_cast<size_t>(kStatPairs) * kStatStages * 2 * row + kStatPairs * kStatXchF2 * sizeof(f2_t) +
+                      (kStatPairs * kStatStages + 1) * sizeof(uint64_t);
+  const int smods = base + kStatModSlots * row <= dev.max_smem_optin;
+  const size_t smem = base + (smods ? kStatModSlots * row : 0);
+  if (smem > dev.max_smem_optin) return cudaErrorInvalidValue;
+  const int nc = row_chunks(a.dim);
+  const bool exact = a.dim == 256 * nc;
+  const int64_t want = (a.rows + kStatPairs - 1) / kStatPairs;
+  const dim3 grid(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
+  auto go = [&](auto kern) -> cudaError_t {
+    cudaError_t e = ensure_smem(kern, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(kern, grid, dim3(kStatWarps * 32), smem, st, a, smods);
   };
-  switch (row_chunks(a.dim)) {
-    case 1: e = go(adaln_bwd_kernel<1, HAS_X, HAS_GZ>); break;
-    case 2: e = go(adaln_bwd_kernel<2, HAS_X, HAS_GZ>); break;
-    case 4: e = go(adaln_bwd_kernel<4, HAS_X, HAS_GZ>); break;
-    case 8: e = go(adaln_bwd_kernel<8, HAS_X, HAS_GZ>); break;
-    default: e = cudaErrorInvalidValue; break;
+#define AFB_LAUNCH_STATS(NC) \
+  return exact ? go(adaln_bwd_stats_kernel<NC, true>) : go(adaln_bwd_stats_kernel<NC, false>)
+  switch (nc) {
+    case 1: AFB_LAUNCH_STATS(1);
+    case 2: AFB_LAUNCH_STATS(2);
+    case 4: AFB_LAUNCH_STATS(4);
+    case 8: AFB_LAUNCH_STATS(8);
+    default: return cudaErrorInvalidValue;
   }
-  return e;
+#undef AFB_LAUNCH_STATS
+}
+
+template <bool HAS_X, bool HAS_GZ>
+static cudaError_t launch_adaln_bwd_cols(const AdalnColsArgs& a, int64_t batch, cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>((a.dim + kColCols - 1) / kColCols), static_cast<unsigned>(a.chunks),
+                  static_cast<unsigned>(batch));
+  return launch_pdl(adaln_bwd_cols_kernel<HAS_X, HAS_GZ>, grid, dim3(kColWarps * 32), 0, st, a);
+}
+
+cudaError_t read_status_adaln_bwd(int* status) {
+  return cudaMemcpyFromSymbol(status, g_afb_device_status, sizeof(int));
+}
+
+static size_t adaln_bwd_stats_bytes(int64_t batch, int64_t seq) {
+  return static_cast<size_t>(batch * seq) * sizeof(float4);
 }
 
 size_t adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim, bool has_x) {
   const int64_t chunks = (seq + kChunkRows - 1) / kChunkRows;
-  return static_cast<size_t>(batch * chunks * (has_x ? 3 : 2) * dim) * sizeof(float);
+  return adaln_bwd_stats_bytes(batch, seq) +
+         static_cast<size_t>(batch * chunks * (has_x ? 3 : 2) * dim) * sizeof(float);
 }
 
 // Shared implementation of the two entry points (and of the workspace-free
@@ -241,27 +380,40 @@ int adaln_bwd_impl(const char* name, const void* gh, const void* gz, const void*
                  " bytes"))
     return g.fail();
   if (batch == 0) return 0;
-  AdalnBwdArgs a{};
-  a.gh = static_cast<const uint16_t*>(gh);
+  const int64_t chunks = (seq + kChunkRows - 1) / kChunkRows;
+  float4* stats = static_cast<float4*>(workspace);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + adaln_bwd_stats_bytes(batch, seq));
+  AdalnStatsArgs sa{};
+  sa.gh = static_cast<const uint16_t*>(gh);
+  sa.z = static_cast<const uint16_t*>(z);
+  sa.scale = static_cast<const uint16_t*>(scale);
+  sa.stats = stats;
+  sa.rows = batch * seq;
+  sa.seq = seq;
+  sa.dim = static_cast<int>(dim);
+  sa.eps = eps;
+  cudaError_t e = launch_adaln_bwd_stats(sa, st);
+  if (e != cudaSuccess) return g.done(e);
+  AdalnColsArgs a{};
+  a.gh = sa.gh;
   a.gz = static_cast<const uint16_t*>(gz);
-  a.z = static_cast<const uint16_t*>(z);
+  a.z = sa.z;
   a.x = static_cast<const uint16_t*>(x);
   a.gate = static_cast<const uint16_t*>(gate);
-  a.scale = static_cast<const uint16_t*>(scale);
+  a.scale = sa.scale;
+  a.stats = stats;
   a.dz = static_cast<uint16_t*>(dz);
   a.dx = static_cast<uint16_t*>(dx);
-  a.part = static_cast<float*>(workspace);
+  a.part = part;
   a.seq = seq;
-  a.chunks = (seq + kChunkRows - 1) / kChunkRows;
+  a.chunks = chunks;
   a.dim = static_cast<int>(dim);
-  a.eps = eps;
-  cudaError_t e;
-  if (has_x) e = gz ? launch_adaln_bwd<true, true>(a, batch, st) : launch_adaln_bwd<true, false>(a, batch, st);
-  else e = gz ? launch_adaln_bwd<false, true>(a, batch, st) : launch_adaln_bwd<false, false>(a, batch, st);
+  if (has_x) e = gz ? launch_adaln_bwd_cols<true, true>(a, batch, st) : launch_adaln_bwd_cols<true, false>(a, batch, st);
+  else e = gz ? launch_adaln_bwd_cols<false, true>(a, batch, st) : launch_adaln_bwd_cols<false, false>(a, batch, st);
   if (e != cudaSuccess) return g.done(e);
   FinalizeArgs f{};
-  f.part = static_cast<const float*>(workspace);
-  f.n = a.chunks;
+  f.part = part;
+  f.n = chunks;
   f.ncols = (has_x ? 3 : 2) * static_cast<int>(dim);
   f.seg = static_cast<int>(dim);
   f.out[0] = dshift;

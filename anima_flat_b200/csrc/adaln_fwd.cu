@@ -72,49 +72,6 @@ __host__ __device__ constexpr size_t adaln_mod_bytes(int64_t dim, bool has_x) {
   return kAdalnModSlots * adaln_slot_bytes(dim, has_x);
 }
 
-// Canonical sum (P = 32) of a row held by the two warps of a pair.  val(i, j)
-// is the fp32 pair (2j, 2j+1) of the lane's i-th vector (vector index
-// c = 2i + h when SPLIT, else i).  The stride tree over the NH local vectors
-// runs in registers (first level fused with val); with SPLIT the last level
-// adds the partner warp's vector from `xch` ([warp][pair][lane]) after the
-// pair barrier.  Both warps return the same sum.
-template <int NH, bool SPLIT, typename F>
-__device__ __forceinline__ float pair_canonical_sum2(F val, f2_t* xch, int h, int lane, int bar_id) {
-  constexpr int H = NH > 1 ? NH / 2 : 1;
-  f2_t p[H][4];
-#pragma unroll
-  for (int i = 0; i < H; ++i) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if constexpr (NH > 1) {
-        p[i][j] = add2(val(i, j), val(i + H, j));
-      } else {
-        p[i][j] = val(i, j);
-      }
-    }
-  }
-#pragma unroll
-  for (int s = H / 2; s >= 1; s >>= 1) {
-#pragma unroll
-    for (int i = 0; i < s; ++i) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) p[i][j] = add2(p[i][j], p[i + s][j]);
-    }
-  }
-  if constexpr (SPLIT) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) xch[(h * 4 + j) * 32 + lane] = p[0][j];
-    named_bar_sync(bar_id, 64);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) p[0][j] = add2(p[0][j], xch[((h ^ 1) * 4 + j) * 32 + lane]);
-  }
-  const f2_t q = add2(add2(p[0][0], p[0][2]), add2(p[0][1], p[0][3]));
-  float r = __fadd_rn(f2lo(q), f2hi(q));
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) r = __fadd_rn(r, __shfl_xor_sync(kFull, r, o));
-  return r;
-}
-
 // EXACT: dim == 256 * NC, so every lane owns NC full vectors (no masking).
 // use_smods: the launch reserved shared memory for the modulation slots.
 template <int NC, bool HAS_X, bool FP8, bool EXACT>

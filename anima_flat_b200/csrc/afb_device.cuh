@@ -255,6 +255,10 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Plain arrival (no transaction bytes): completes the phase of a count-1 barrier.
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
@@ -401,6 +405,105 @@ __device__ __forceinline__ float warp_canonical_sum2_fn(F val) {
     }
   }
   return warp_canonical_sum2<H>(p);
+}
+
+// Canonical sum (P = 32) of a row held by the two warps of a pair.  val(i, j)
+// is the fp32 pair (2j, 2j+1) of the lane's i-th vector (vector index
+// c = 2i + h when SPLIT, else i).  The stride tree over the NH local vectors
+// runs in registers (first level fused with val); with SPLIT the last level
+// adds the partner warp's vector from `xch` ([warp][pair][lane]) after the
+// pair barrier.  Both warps return the same sum.
+template <int NH, bool SPLIT, typename F>
+__device__ __forceinline__ float pair_canonical_sum2(F val, f2_t* xch, int h, int lane, int bar_id) {
+  constexpr int H = NH > 1 ? NH / 2 : 1;
+  f2_t p[H][4];
+#pragma unroll
+  for (int i = 0; i < H; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (NH > 1) {
+        p[i][j] = add2(val(i, j), val(i + H, j));
+      } else {
+        p[i][j] = val(i, j);
+      }
+    }
+  }
+#pragma unroll
+  for (int s = H / 2; s >= 1; s >>= 1) {
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[i][j] = add2(p[i][j], p[i + s][j]);
+    }
+  }
+  if constexpr (SPLIT) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xch[(h * 4 + j) * 32 + lane] = p[0][j];
+    named_bar_sync(bar_id, 64);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) p[0][j] = add2(p[0][j], xch[((h ^ 1) * 4 + j) * 32 + lane]);
+  }
+  const f2_t q = add2(add2(p[0][0], p[0][2]), add2(p[0][1], p[0][3]));
+  float r = __fadd_rn(f2lo(q), f2hi(q));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) r = __fadd_rn(r, __shfl_xor_sync(kFull, r, o));
+  return r;
+}
+
+// Two canonical sums at once (one exchange and one pair barrier): val(n, i, j)
+// for n = 0, 1; `xch` holds 2 * (2 warps x 4 pairs x 32 lanes).  Same order as
+// pair_canonical_sum2 for each sum.
+template <int NH, bool SPLIT, typename F>
+__device__ __forceinline__ void pair_canonical_sum2x2(F val, f2_t* xch, int h, int lane, int bar_id,
+                                                      float& s0, float& s1) {
+  constexpr int H = NH > 1 ? NH / 2 : 1;
+  f2_t p[2][H][4];
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if constexpr (NH > 1) {
+          p[n][i][j] = add2(val(n, i, j), val(n, i + H, j));
+        } else {
+          p[n][i][j] = val(n, i, j);
+        }
+      }
+    }
+#pragma unroll
+    for (int s = H / 2; s >= 1; s >>= 1) {
+#pragma unroll
+      for (int i = 0; i < s; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[n][i][j] = add2(p[n][i][j], p[n][i + s][j]);
+      }
+    }
+  }
+  if constexpr (SPLIT) {
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xch[((n * 2 + h) * 4 + j) * 32 + lane] = p[n][0][j];
+    named_bar_sync(bar_id, 64);
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[n][0][j] = add2(p[n][0][j], xch[((n * 2 + (h ^ 1)) * 4 + j) * 32 + lane]);
+  }
+  float r[2];
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+    const f2_t q = add2(add2(p[n][0][0], p[n][0][2]), add2(p[n][0][1], p[n][0][3]));
+    r[n] = __fadd_rn(f2lo(q), f2hi(q));
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    r[0] = __fadd_rn(r[0], __shfl_xor_sync(kFull, r[0], o));
+    r[1] = __fadd_rn(r[1], __shfl_xor_sync(kFull, r[1], o));
+  }
+  s0 = r[0];
+  s1 = r[1];
 }
 
 // ---------------------------------------------------------------------------

@@ -39,8 +39,8 @@ def test_signature_table_covers_compute_entry_points():
 def test_workspace_queries():
     lib = _lib.load()
     # [B][chunks of 16 rows][3][D] fp32
-    assert lib.afb_residual_adaln_bwd_workspace(1, 4096, 2048) == 1 * 256 * 3 * 2048 * 4
-    assert lib.afb_adaln_bwd_workspace(2, 17, 256) == 2 * 2 * 2 * 256 * 4
+    assert lib.afb_residual_adaln_bwd_workspace(1, 4096, 2048) == 4096 * 16 + 1 * 256 * 3 * 2048 * 4
+    assert lib.afb_adaln_bwd_workspace(2, 17, 256) == 2 * 17 * 16 + 2 * 2 * 2 * 256 * 4
     # [chunks of 8 tokens][sections][128] fp32
     assert lib.afb_qkv_norm_rope_bwd_workspace(1, 4096, 16, 128) == 512 * 2 * 128 * 4
     assert lib.afb_head_norm_bwd_workspace(1, 4096, 16, 128) == 512 * 1 * 128 * 4
