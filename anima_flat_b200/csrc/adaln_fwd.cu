@@ -55,7 +55,14 @@ struct AdalnArgs {
 
 constexpr int kAdalnPairs = 8;
 constexpr int kAdalnWarps = 2 * kAdalnPairs;
-constexpr int kAdalnMaxStages = 2;  // more stages delay each pair's first row behind the others' copies
+// Stages per pair.  A short launch (few rows per SM: config 2 has 27.7) is
+// mostly ramp and tail, and more stages delay each pair's first row behind the
+// others' copies, so it takes two.  A long launch is a steady stream, where the
+// bytes in flight bound the bandwidth, so it takes the deepest ring that fits,
+// giving up the shared-memory modulation slots if that buys a stage.
+constexpr int kAdalnShortStages = 2;
+constexpr int kAdalnMaxStages = 4;
+constexpr int64_t kAdalnLongRowsPerCta = 128;
 // Per pair: two exchange buffers (one per sum of a row) of 2 warps x 4 pairs
 // of fp32 x 32 lanes, then two floats for the FP8 row max (padded to 16 B).
 constexpr size_t kAdalnXchF2 = 2 * 2 * 4 * 32;
@@ -76,7 +83,7 @@ __host__ __device__ constexpr size_t adaln_mod_bytes(int64_t dim, bool has_x) {
 // use_smods: the launch reserved shared memory for the modulation slots.
 template <int NC, bool HAS_X, bool FP8, bool EXACT>
 __global__ void __launch_bounds__(kAdalnWarps * 32, 1)
-adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods) {
+adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const int early) {
   // SPLIT: the pair divides each lane's vectors; for NC == 1 both warps hold
   // the single vector and warp 0 writes the outputs.
   constexpr bool SPLIT = NC >= 2;
@@ -191,6 +198,13 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods) {
         zv[i] = ok(i) ? lds16(st + col(i) * 2) : make_uint4(0, 0, 0, 0);
         if (HAS_X) xv[i] = ok(i) ? lds16(st + row_bytes + col(i) * 2) : make_uint4(0, 0, 0, 0);
       }
+      if (early) {  // refill as soon as both warps hold the row (long launches)
+        named_bar_sync(bar_id, 64);
+        if (leader && !dead && row_of(j + nsw) < r1) {
+          fence_proxy_async_smem();
+          issue(j + nsw);
+        }
+      }
       if (HAS_X) {
 #pragma unroll
         for (int i = 0; i < NH; ++i) {
@@ -219,10 +233,12 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods) {
     const float mean = div_d(pair_canonical_sum2<NH, SPLIT>(
         [&](int i, int jj) { return zf[i][jj]; }, xch, h, lane, bar_id));
     // Both warps have read the stage (the pair barrier above): refill it.
-    if (!SPLIT) named_bar_sync(bar_id, 64);
-    if (leader && !dead && row_of(j + nsw) < r1) {
-      fence_proxy_async_smem();
-      issue(j + nsw);
+    if (!early) {
+      if (!SPLIT) named_bar_sync(bar_id, 64);
+      if (leader && !dead && row_of(j + nsw) < r1) {
+        fence_proxy_async_smem();
+        issue(j + nsw);
+      }
     }
     const f2_t mm = f2(mean, mean);
 #pragma unroll
@@ -302,18 +318,24 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods) {
 struct AdalnPlan {
   int nsw;
   int smods;
+  int early;  // refill a stage right after the pair has read it (one more pair barrier per row)
   size_t smem;
 };
-static AdalnPlan adaln_plan(int64_t dim, bool has_x, size_t limit) {
+static AdalnPlan adaln_plan(int64_t dim, bool has_x, size_t limit, bool long_launch) {
   const size_t per = kAdalnPairs * ((has_x ? 2 : 1) * static_cast<size_t>(dim) * 2 + sizeof(uint64_t));
   const size_t xch = kAdalnPairs * kAdalnPairXchBytes + sizeof(uint64_t);
   const size_t mods = adaln_mod_bytes(dim, has_x);
+  const int cap = long_launch ? kAdalnMaxStages : kAdalnShortStages;
+  auto stages = [&](size_t fixed) {
+    const int n = limit > fixed ? static_cast<int>((limit - fixed) / per) : 0;
+    return n < cap ? n : cap;
+  };
   AdalnPlan p{};
-  p.smods = xch + mods + per <= limit;
-  const size_t fixed = xch + (p.smods ? mods : 0);
-  const int n = limit > fixed ? static_cast<int>((limit - fixed) / per) : 0;
-  p.nsw = n < 1 ? 1 : (n > kAdalnMaxStages ? kAdalnMaxStages : n);
-  p.smem = fixed + p.nsw * per;
+  const int with = stages(xch + mods), without = stages(xch);
+  p.smods = with >= 1 && with >= without;
+  p.nsw = p.smods ? with : (without < 1 ? 1 : without);
+  p.smem = xch + (p.smods ? mods : 0) + p.nsw * per;
+  p.early = long_launch && has_x;  // measured: helps the residual stream, not plain adaln
   return p;
 }
 
@@ -323,14 +345,15 @@ static cudaError_t launch_adaln(const AdalnArgs& a, cudaStream_t st) {
   if (dev.error != cudaSuccess) return dev.error;
   const int nc = row_chunks(a.dim);
   const bool exact = a.dim == 256 * nc;
-  const AdalnPlan plan = adaln_plan(a.dim, HAS_X, dev.max_smem_optin);
   const int64_t want = (a.rows + kAdalnPairs - 1) / kAdalnPairs;
   const dim3 grid(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
+  const AdalnPlan plan = adaln_plan(a.dim, HAS_X, dev.max_smem_optin,
+                                    a.rows >= kAdalnLongRowsPerCta * static_cast<int64_t>(grid.x));
   const dim3 block(kAdalnWarps * 32);
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e = ensure_smem(kern, plan.smem);
     if (e != cudaSuccess) return e;
-    return launch_pdl(kern, grid, block, plan.smem, st, a, plan.nsw, plan.smods);
+    return launch_pdl(kern, grid, block, plan.smem, st, a, plan.nsw, plan.smods, plan.early);
   };
 #define AFB_LAUNCH_ADALN(NC)                                            \
   return exact ? go(adaln_fwd_kernel<NC, HAS_X, FP8, true>) \

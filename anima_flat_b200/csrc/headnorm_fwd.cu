@@ -15,8 +15,9 @@
 // is one section of one token: its q or its k heads (normed, rotated), or its
 // v (copied, grad mode); unit u is section u % NU of token u / NU.  Warp w of
 // CTA c owns the units w*G + c + k*G*W (G CTAs of W warps: every SM gets the
-// same share), with a private ring of shared-memory stages (two measured best:
-// more stages delay each warp's first unit behind the others' copies).  Lane 0 streams
+// same share), with a private ring of shared-memory stages: two for a short
+// launch (more delay each warp's first unit behind the others' copies), as
+// many as fit for a long one (a steady stream, bound by the bytes in flight).  Lane 0 streams
 // each unit into a stage with bulk copies (TMA engine) completing on the
 // stage's mbarrier: the section, and for a rotated section the token's cos and
 // sin rows, so no per-token global load sits on the critical path.  The norm
@@ -52,7 +53,9 @@ struct HeadNormArgs {
 };
 
 constexpr int kHeadWarps = 16;
-constexpr int kHeadMaxStages = 2;
+constexpr int kHeadShortStages = 2;
+constexpr int kHeadMaxStages = 4;
+constexpr int64_t kHeadLongUnitsPerCta = 256;
 constexpr int kHeadUnroll = 4;
 
 template <int HD, bool ROTATE, bool WITH_K, bool WITH_V>
@@ -240,13 +243,14 @@ static cudaError_t launch_headnorm(const HeadNormArgs& a, int hd, cudaStream_t s
   const size_t stage = static_cast<size_t>(a.heads) * hd * 2 + (ROTATE ? static_cast<size_t>(hd) * 4 : 0);
   const size_t per = kHeadWarps * (stage + sizeof(uint64_t));
   const size_t fixed = static_cast<size_t>(WITH_K ? 2 : 1) * hd * sizeof(float) + sizeof(uint64_t);
-  int nsw = static_cast<int>((dev.max_smem_optin - fixed) / per);
-  if (nsw < 1) return cudaErrorInvalidValue;  // caller bounds heads * head_dim
-  if (nsw > kHeadMaxStages) nsw = kHeadMaxStages;
-  const size_t smem = fixed + per * nsw;
   const int64_t units = a.tokens * ((WITH_K ? 2 : 1) + (WITH_V ? 1 : 0));
   const int64_t want = (units + kHeadWarps - 1) / kHeadWarps;
   const dim3 grid(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
+  const int cap = units >= kHeadLongUnitsPerCta * static_cast<int64_t>(grid.x) ? kHeadMaxStages : kHeadShortStages;
+  int nsw = static_cast<int>((dev.max_smem_optin - fixed) / per);
+  if (nsw < 1) return cudaErrorInvalidValue;  // caller bounds heads * head_dim
+  if (nsw > cap) nsw = cap;
+  const size_t smem = fixed + per * nsw;
   const dim3 block(kHeadWarps * 32);
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e = ensure_smem(kern, smem);

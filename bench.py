@@ -628,7 +628,7 @@ def run_per_op(args):
     names = PER_OPS if args.op == "all" else args.op.split(",")
     for name in names:
         fp8 = name in ("residual_adaln_fp8", "adaln_fp8", "rowquant", "rowquant_gelu")
-        s = W.Shape(batch=2 if fp8 else 1)
+        s = W.Shape(batch=args.op_batch or (2 if fp8 else 1))
         B, S, D, H, hd = s.batch, s.seq, s.dim, s.heads, s.head_dim
         g = torch.Generator(device=device).manual_seed(7)
         act = lambda *d: torch.randn(*d, generator=g, device=device).to(torch.bfloat16)
@@ -734,6 +734,8 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--op", default=None,
                     help="per-op table instead of the step: 'all' or comma-separated op names")
+    ap.add_argument("--op-batch", type=int, default=0,
+                    help="batch of the per-op shapes (default: the op's config, 1 or 2)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_info()

@@ -44,8 +44,12 @@ def dev(a, cuda_dev):
 
 # (64, 1, 2048) and (40, 3, 1024): CTAs whose rows span more than two batch
 # entries read the modulation from global memory instead of shared memory.
+# (3, 8192, 512) and (5, 4096, 2048): long launches (>= 128 rows per CTA),
+# which take the deep ring; at D = 2048 the residual one gives up the
+# shared-memory modulation slots for it.
 ADALN_SHAPES = [(1, 1, 2048), (2, 3, 2048), (1, 4096, 2048), (2, 37, 1024), (3, 5, 256),
-                (1, 7, 4096), (1, 9, 8), (2, 11, 2040), (1, 3, 520), (64, 1, 2048), (40, 3, 1024)]
+                (1, 7, 4096), (1, 9, 8), (2, 11, 2040), (1, 3, 520), (64, 1, 2048), (40, 3, 1024),
+                (3, 8192, 512), (5, 4096, 2048)]
 
 
 @pytest.mark.parametrize("B,S,D", ADALN_SHAPES)
@@ -70,7 +74,8 @@ def test_adaln_bit_exact(B, S, D, cuda_dev):
 
 
 @pytest.mark.parametrize("B,S,D", [(1, 1, 2048), (2, 4096, 2048), (2, 37, 1024), (3, 5, 256),
-                                   (1, 7, 4096), (2, 11, 2040), (64, 1, 2048), (40, 3, 1024)])
+                                   (1, 7, 4096), (2, 11, 2040), (64, 1, 2048), (40, 3, 1024),
+                                   (3, 8192, 512)])
 @pytest.mark.parametrize("has_x", [True, False])
 def test_adaln_fp8_bit_exact(B, S, D, has_x, cuda_dev):
     r = rng(B * 3000 + S + D + has_x)
@@ -227,8 +232,10 @@ def test_gelu_probe_exhaustive(cuda_dev):
     assert np.all(np.abs(f - c) <= bound)
 
 
+# (1, 19000, 4, 128): a long launch (>= 256 units per CTA, deep ring).
 QKV_CASES = [(1, 4096, 16, 128, 1e-5), (2, 16, 4, 128, 1e-5), (1, 6, 3, 64, 1e-6),
-             (1, 5, 2, 256, 1e-5), (2, 7, 5, 128, 1e-6), (3, 1, 16, 128, 1e-5)]
+             (1, 5, 2, 256, 1e-5), (2, 7, 5, 128, 1e-6), (3, 1, 16, 128, 1e-5),
+             (1, 19000, 4, 128, 1e-5)]
 
 
 def qkv_inputs(r, B, S, H, hd):
@@ -257,7 +264,8 @@ def test_qkv_norm_rope_bit_exact(B, S, H, hd, eps, cuda_dev):
     np.testing.assert_array_equal(to_bits(v2), qkv.reshape(B, S, 3, H, hd)[:, :, 2])
 
 
-@pytest.mark.parametrize("B,S,H,hd", [(1, 4096, 16, 128), (2, 5, 4, 128), (1, 3, 7, 64), (2, 2, 3, 256)])
+@pytest.mark.parametrize("B,S,H,hd", [(1, 4096, 16, 128), (2, 5, 4, 128), (1, 3, 7, 64), (2, 2, 3, 256),
+                                      (1, 38000, 2, 64)])
 def test_head_norm_bit_exact(B, S, H, hd, cuda_dev):
     r = rng(B * 11 + S + H + hd)
     x = act(r, (B, S, H * hd))
