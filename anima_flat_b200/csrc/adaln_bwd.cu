@@ -428,8 +428,8 @@ int adaln_bwd_impl(const char* name, const void* gh, const void* gz, const void*
 // cannot allocate device memory at all (a host binding with no device
 // allocator of its own, or a serving process whose device memory is fully
 // reserved at start-up and which forbids allocation on the hot path).  For
-// them the parameter-gradient partials live in this file-scope array
-// instead of a caller-provided workspace.  Every GPU that loads the library
+// them the workspace (row statistics and parameter-gradient partials) lives
+// in this file-scope array instead of a caller-provided one.  Every GPU that loads the library
 // holds these 16 MiB until the process exits.
 // ---------------------------------------------------------------------------
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
@@ -464,10 +464,10 @@ using namespace afb;
 
 // Allocation-free variant of afb_residual_adaln_bwd (see the scratch comment
 // above).  The first call on a device looks up the scratch address; make that
-// first call before any stream capture.  The partial sums it keeps there are
-// fully overwritten by every call, so nothing needs clearing, but all calls
-// share the one array: calls that overlap on the GPU (other streams, other
-// threads) race.  Sizes whose partials exceed 16 MiB are rejected.
+// first call before any stream capture.  What it keeps there is fully
+// overwritten by every call, so nothing needs clearing, but all calls share
+// the one array: calls that overlap on the GPU (other streams, other threads)
+// race.  Sizes whose workspace exceeds 16 MiB are rejected.
 extern "C" int afb_residual_adaln_bwd_noalloc(const void* gh, const void* gz, const void* z,
                                               const void* x, const void* gate, const void* scale,
                                               void* dx, void* dres, void* dgate, void* dshift,

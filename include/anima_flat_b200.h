@@ -123,7 +123,8 @@ int afb_head_norm(const void* x, const void* weight, void* y, int64_t batch,
 /* ----------------------------------------------------------------------- */
 /* Each backward entry point takes a caller-provided device workspace of at
  * least the size its *_workspace query returns (fp32 partial sums of the
- * parameter gradients); it is fully overwritten and needs no zeroing.  The
+ * parameter gradients, and for the AdaLN backward 16 bytes of row statistics
+ * per row); it is fully overwritten and needs no zeroing.  The
  * parameter gradients are summed in a fixed order, so they are reproducible
  * from run to run and across GPUs. */
 
@@ -144,8 +145,8 @@ int afb_residual_adaln_bwd(const void* gh, const void* gz, const void* z, const 
  * hot path).  It has no counterpart in the reference.  Same arguments and
  * outputs, without the workspace: the partial sums live in a 16 MiB array
  * inside the library, which every GPU that loads the library holds until
- * exit.  Sizes needing more (batch * ceil(seq/16) * 3 * dim * 4 bytes) are
- * rejected.  The first call on a device resolves the array's address; make
+ * exit.  Sizes needing more (batch * seq * 16 + batch * ceil(seq/16) * 3 *
+ * dim * 4 bytes, the workspace query's value) are rejected.  The first call on a device resolves the array's address; make
  * it before any stream capture.  All calls share the array: calls that
  * overlap on the GPU race. */
 int afb_residual_adaln_bwd_noalloc(const void* gh, const void* gz, const void* z,
