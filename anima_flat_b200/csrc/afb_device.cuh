@@ -572,4 +572,35 @@ __device__ __forceinline__ float fast_gelu(float x) {
   return x * __fmaf_rn(0.5f, copysignf(y, x), 0.5f);
 }
 
+// fast_gelu on a pair of elements with packed fp32x2 arithmetic: the same
+// operations lane by lane (fma.rn.f32x2 and mul.rn.f32x2 round like the
+// scalar fma and mul; the reciprocal and the exponential stay scalar), so the
+// result is bit-identical to fast_gelu on each element.  It has no product
+// feeding an add, so the packed contraction rule does not apply.
+__device__ __forceinline__ f2_t fma2(f2_t a, f2_t b, f2_t c) {
+  f2_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ f2_t splat2(float v) { return f2(v, v); }
+__device__ __forceinline__ f2_t fast_gelu2(f2_t x) {
+  constexpr f2_t kAbs = 0x7fffffff7fffffffull, kSign = 0x8000000080000000ull;
+  const f2_t den = fma2(x & kAbs, splat2(0.3275911f * 0.707106769084930419921875f), splat2(1.0f));
+  float t0, t1;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(f2lo(den)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(f2hi(den)));
+  const f2_t t = f2(t0, t1);
+  f2_t p = fma2(splat2(1.061405429f), t, splat2(-1.453152027f));
+  p = fma2(p, t, splat2(1.421413741f));
+  p = fma2(p, t, splat2(-0.284496736f));
+  p = fma2(p, t, splat2(0.254829592f));
+  p = mul2(p, t);
+  const f2_t arg = mul2(mul2(x, x), splat2(-0.721347520444481703680f));
+  float e0, e1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(f2lo(arg)));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(f2hi(arg)));
+  const f2_t y = fma2(p ^ kSign, f2(e0, e1), splat2(1.0f));  // 1 - p*e
+  return mul2(x, fma2(splat2(0.5f), (y & kAbs) | (x & kSign), splat2(0.5f)));  // copysign(y, x)
+}
+
 }  // namespace afb

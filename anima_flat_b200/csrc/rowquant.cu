@@ -55,7 +55,8 @@ rowquant_kernel(const RowquantArgs a) {
   const int K = a.K;
   const int64_t base = (row_ok ? row : 0) * K;
 
-  float y[CPL][16];
+  // y as fp32 pairs: y2[c][j] holds elements (2j, 2j+1) of chunk c.
+  f2_t y2[CPL][8];
   float amax = 0.0f;
   {
     uint4 xv[CPL][2];
@@ -68,16 +69,12 @@ rowquant_kernel(const RowquantArgs a) {
     }
 #pragma unroll
     for (int c = 0; c < CPL; ++c) {
-      float lo[8], hi[8];
-      unpack8(xv[c][0], lo);
-      unpack8(xv[c][1], hi);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        y[c][k] = GELU ? fast_gelu(lo[k]) : lo[k];
-        y[c][k + 8] = GELU ? fast_gelu(hi[k]) : hi[k];
+      for (int j = 0; j < 8; ++j) {
+        const f2_t v = bf2f2(word(xv[c][j >> 2], j & 3));
+        y2[c][j] = GELU ? fast_gelu2(v) : v;
+        amax = fmaxf(amax, fmaxf(fabsf(f2lo(y2[c][j])), fabsf(f2hi(y2[c][j]))));
       }
-#pragma unroll
-      for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(y[c][k]));
     }
   }
   const float lamax = amax;
@@ -110,7 +107,8 @@ rowquant_kernel(const RowquantArgs a) {
         const int e = (t + 32 * GROUP * c) * 16;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          if (fabsf(y[c][k]) >= thresh) {
+          const float yk = (k & 1) ? f2hi(y2[c][k >> 1]) : f2lo(y2[c][k >> 1]);
+          if (fabsf(yk) >= thresh) {
             const float xk = __uint_as_float(static_cast<uint32_t>(__ldg(a.x + base + e + k)) << 16);
             exact = fmaxf(exact, fabsf(canonical_gelu_call(xk)));
           }
@@ -127,22 +125,26 @@ rowquant_kernel(const RowquantArgs a) {
   for (int c = 0; c < CPL; ++c) {
     const int e = (t + 32 * GROUP * c) * 16;
     if (e < K) {
-      float lo[8], hi[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        lo[k] = y[c][k];
-        hi[k] = y[c][k + 8];
-      }
       uint2 plo, phi;
       if (GELU) {
+        const f2_t rr = f2(r, r);
+        uint32_t w[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          lo[k] = clamp448(__fmul_rn(lo[k], r));
-          hi[k] = clamp448(__fmul_rn(hi[k], r));
+        for (int j = 0; j < 8; ++j) {
+          const f2_t q = mul2(y2[c][j], rr);
+          w[j] = e4m3x2(clamp448(f2lo(q)), clamp448(f2hi(q)));
         }
-        plo = e4m3x8(lo);
-        phi = e4m3x8(hi);
+        plo = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
+        phi = make_uint2(w[4] | (w[5] << 16), w[6] | (w[7] << 16));
       } else {
+        float lo[8], hi[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          lo[2 * k] = f2lo(y2[c][k]);
+          lo[2 * k + 1] = f2hi(y2[c][k]);
+          hi[2 * k] = f2lo(y2[c][k + 4]);
+          hi[2 * k + 1] = f2hi(y2[c][k + 4]);
+        }
         plo = e4m3_quot8(lo, s, r);
         phi = e4m3_quot8(hi, s, r);
       }
@@ -189,11 +191,15 @@ static cudaError_t launch_rowquant(const RowquantArgs& a, cudaStream_t st) {
 
 // Elementwise fast and canonical GELU, for checking the fast_gelu error bound
 // that the GELU row kernel relies on.
+// The fast values come from fast_gelu2, the pairwise form the row kernel runs.
 __global__ void gelu_probe_kernel(const uint16_t* x, float* fast, float* canon, int64_t n) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float v = __uint_as_float(static_cast<uint32_t>(x[i]) << 16);
-  fast[i] = fast_gelu(v);
+  const int64_t partner = (i ^ 1) < n ? (i ^ 1) : i;  // the other lane of the pair
+  const float w = __uint_as_float(static_cast<uint32_t>(x[partner]) << 16);
+  const f2_t g = fast_gelu2(f2(v, w));
+  fast[i] = f2lo(g);
   canon[i] = canonical_gelu(v);
 }
 
