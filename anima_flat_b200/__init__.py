@@ -1,16 +1,18 @@
 """anima_flat_b200 — the fused DiT layer ops of anima-flat, hand-written for B200 (sm_100a).
 
-Public functions mirror src/kernels/{adaln,fp8,rope}.py of the reference:
+Public functions mirror src/kernels/{adaln,fp8,rope,ctx_scale}.py of the reference:
 
     adaln, residual_adaln                         (AdaLN modulate, gated residual)
     adaln_fp8, residual_adaln_fp8, rowquant       (per-row FP8 e4m3 quantisation)
     qkv_norm_rope, head_norm                      (q/k RMSNorm + 3D RoPE)
+    ctx_scale                                     (trimmed cross-attention gain)
 
 All run through the C-ABI library ``lib/libanima_flat_b200.so`` (see
 ``include/anima_flat_b200.h``); there is no CPU fallback.
 """
 
 from .kernels.adaln import adaln, residual_adaln
+from .kernels.ctx_scale import ctx_scale
 from .kernels.fp8 import FP8, FP8_MAX, adaln_fp8, residual_adaln_fp8, rowquant
 from .kernels.rope import head_norm, qkv_norm_rope
 from .tables import rope_tables
@@ -20,6 +22,7 @@ __all__ = [
     "FP8_MAX",
     "adaln",
     "adaln_fp8",
+    "ctx_scale",
     "head_norm",
     "qkv_norm_rope",
     "residual_adaln",

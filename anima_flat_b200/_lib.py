@@ -38,6 +38,8 @@ SIGNATURES: dict[str, tuple] = {
     "afb_qkv_norm_rope_bwd": (_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P,
                               ctypes.c_size_t, _P),
     "afb_head_norm_bwd": (_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, ctypes.c_size_t, _P),
+    "afb_ctx_scale": (_P, _P, _P, _P, _I, _I, _I, _I, _P),
+    "afb_ctx_scale_bwd": (_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P),
 }
 
 # Workspace-size queries: name -> argument types (return size_t).

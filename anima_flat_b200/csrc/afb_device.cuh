@@ -533,6 +533,31 @@ __device__ __forceinline__ float canonical_exp_nonpos(float a) {
                    __int_as_float((-64 + 127) << 23));
 }
 
+// exp(a) for every fp32 a, by the same reduction and polynomial as
+// canonical_exp_nonpos (identical results for a <= 0).  Above 2^127 the scale
+// is applied in two exact steps; beyond exp's range the product overflows to
+// infinity as IEEE multiplication does; NaN propagates.
+__device__ __forceinline__ float canonical_exp(float a) {
+  if (a != a) return a + a;
+  if (a < -104.0f) return 0.0f;
+  if (a > 88.8f) return __int_as_float(0x7f800000);
+  const float k = rintf(__fmul_rn(a, 1.44269502162933349609375f));
+  float r = __fmaf_rn(k, -0.693145751953125f, a);
+  r = __fmaf_rn(k, -1.428606765330187e-06f, r);
+  float p = 1.98412701138295233249664306640625e-04f;
+  p = __fmaf_rn(p, r, 1.38888892251998186111450195312500e-03f);
+  p = __fmaf_rn(p, r, 8.33333376795053482055664062500000e-03f);
+  p = __fmaf_rn(p, r, 4.16666679084300994873046875000000e-02f);
+  p = __fmaf_rn(p, r, 1.66666671633720397949218750000000e-01f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int ki = static_cast<int>(k);
+  if (ki > 127) return __fmul_rn(__fmul_rn(p, __int_as_float((64 + 127) << 23)), __int_as_float((ki - 64 + 127) << 23));
+  if (ki >= -125) return __fmul_rn(p, __int_as_float((ki + 127) << 23));
+  return __fmul_rn(__fmul_rn(p, __int_as_float((ki + 64 + 127) << 23)), __int_as_float((-64 + 127) << 23));
+}
+
 __device__ __forceinline__ float canonical_gelu(float x) {
   const float z = __fmul_rn(x, 0.707106769084930419921875f);
   const float az = fabsf(z);

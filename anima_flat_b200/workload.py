@@ -85,6 +85,16 @@ def bytes_head_norm_bwd(s: Shape) -> int:
     return s.rows * 3 * w * 2 + 2 * s.head_dim * 4
 
 
+def bytes_ctx_scale(s: Shape) -> int:
+    # out read, y written; lse [B, H, S] fp32 read; ln_pad [B]
+    return s.rows * s.heads * s.head_dim * 2 * 2 + s.rows * s.heads * 4 + s.batch * 4
+
+
+def bytes_ctx_scale_bwd(s: Shape) -> int:
+    # out, dy read, dout written; lse read, dlse written; ln_pad
+    return s.rows * s.heads * s.head_dim * 2 * 3 + s.rows * s.heads * 4 * 2 + s.batch * 4
+
+
 def bf16_forward_calls(s: Shape) -> list[str]:
     """Op names in call order for forward_fused (model.py:366-375)."""
     calls = ["adaln"]
@@ -122,6 +132,8 @@ def call_bytes(name: str, s: Shape) -> int:
         "adaln_bwd": bytes_adaln_bwd,
         "qkv_norm_rope_bwd": bytes_qkv_norm_rope_bwd,
         "head_norm_bwd": bytes_head_norm_bwd,
+        "ctx_scale": bytes_ctx_scale,
+        "ctx_scale_bwd": bytes_ctx_scale_bwd,
     }[name](s)
 
 

@@ -609,7 +609,7 @@ def run_reference(args, world, rank):
 # ------------------------------------------------------------- per-op table --
 PER_OPS = ["residual_adaln", "adaln", "qkv_norm_rope", "head_norm", "residual_adaln_fp8",
            "adaln_fp8", "rowquant", "rowquant_gelu", "residual_adaln_bwd", "adaln_bwd",
-           "qkv_norm_rope_bwd", "head_norm_bwd"]
+           "qkv_norm_rope_bwd", "head_norm_bwd", "ctx_scale", "ctx_scale_bwd"]
 
 
 def run_per_op(args):
@@ -667,6 +667,16 @@ def run_per_op(args):
             ops = torch.ops.anima_flat_b200
             sets = [(act(B, S, H * hd), act(B, S, H, hd) * 0.01, w, H, 1e-5) for _ in range(nbuf)]
             fn = ops.head_norm_bwd
+        elif name in ("ctx_scale", "ctx_scale_bwd"):  # cross-attention output at config 2
+            lse = lambda: 2.0 + 4.0 * torch.randn(B, H, S, generator=g, device=device)
+            lnp = torch.full((B,), 4.0, device=device)
+            if name == "ctx_scale":
+                sets = [(act(B, S, H, hd), lse(), lnp) for _ in range(nbuf)]
+                fn = afb.ctx_scale
+            else:
+                ops = torch.ops.anima_flat_b200
+                sets = [(act(B, S, H, hd), lse(), lnp, act(B, S, H, hd) * 0.01) for _ in range(nbuf)]
+                fn = ops.ctx_scale_bwd
         else:
             K = s.mlp if name == "rowquant_gelu" else D
             sets = [(act(B, S, K),) for _ in range(nbuf)]

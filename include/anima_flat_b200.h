@@ -118,6 +118,14 @@ int afb_head_norm(const void* x, const void* weight, void* y, int64_t batch,
                   int64_t seq, int64_t heads, int64_t head_dim, float eps,
                   void* stream);
 
+/* Replaces src/kernels/ctx_scale.py:40-57 (anima_flat::ctx_scale, launching
+ * _ctx_scale_kernel, ctx_scale.py:8-37), called from src/attention.py:180.
+ * out, y [batch, seq, heads, head_dim] bf16; lse [batch, heads, seq] fp32;
+ * ln_pad [batch] fp32.  y = bf16(out * gain), gain = 1 / (1 + exp(ln_pad -
+ * lse)).  head_dim in {64, 128, 256}, heads * head_dim <= 2048. */
+int afb_ctx_scale(const void* out, const void* lse, const void* ln_pad, void* y, int64_t batch,
+                  int64_t seq, int64_t heads, int64_t head_dim, void* stream);
+
 /* ----------------------------------------------------------------------- */
 /* Backward (LoRA training)                                                 */
 /* ----------------------------------------------------------------------- */
@@ -182,6 +190,14 @@ size_t afb_head_norm_bwd_workspace(int64_t batch, int64_t seq, int64_t heads,
 int afb_head_norm_bwd(const void* x, const void* dy, const void* weight, void* dx, void* dw,
                       int64_t batch, int64_t seq, int64_t heads, int64_t head_dim, float eps,
                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces src/kernels/ctx_scale.py:103-120 (anima_flat::ctx_scale_bwd,
+ * launching _ctx_scale_bwd_kernel, ctx_scale.py:61-100): dout = bf16(dy *
+ * gain) [batch, seq, heads, head_dim]; dlse = sum(dy * out) * gain *
+ * (1 - gain) [batch, heads, seq] fp32. */
+int afb_ctx_scale_bwd(const void* out, const void* lse, const void* ln_pad, const void* dy,
+                      void* dout, void* dlse, int64_t batch, int64_t seq, int64_t heads,
+                      int64_t head_dim, void* stream);
 
 #ifdef __cplusplus
 }

@@ -35,6 +35,8 @@ def lib():
             "orc_adaln_bwd": ([P] * 11 + [I, I, I, F, N, N, N], None),
             "orc_headnorm_bwd": ([P, I, I, I, I] + [P] * 10 + [I, I, I, I, F, N, N, N, N, N], None),
             "orc_e4m3_to_f32": ([ctypes.c_uint8], c_float),
+            "orc_exp": ([c_float], c_float),
+            "orc_ctx_scale": ([P] * 7 + [I, I, I, I, N], None),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(L, name)
@@ -189,3 +191,25 @@ def head_norm_bwd(x, dy, w, heads, eps=1e-5, mode=RNE):
                            None, _p(dx), _p(dw), None, B * S, S, heads, hd, eps, 0, 1, HN_WARPS,
                            HN_TOK_PER_WARP, mode)
     return dx, dw
+
+
+def exp(a: float) -> float:
+    """The canonical fp32 exp (Cody-Waite reduction, degree-7 Taylor)."""
+    return float(lib().orc_exp(float(a)))
+
+
+def ctx_scale(out, lse, ln_pad, dy=None, mode=RNE):
+    """ctx_scale forward (dy None: returns y) or backward (returns dout, dlse).
+    out/dy: [B,S,H,hd] bf16 bits; lse: [B,H,S] fp32; ln_pad: [B] fp32."""
+    out = u16(out)
+    B, S, H, hd = out.shape
+    lse, ln_pad = f32(lse), f32(ln_pad)
+    if dy is None:
+        y = np.empty_like(out)
+        lib().orc_ctx_scale(_p(out), _p(lse), _p(ln_pad), None, _p(y), None, None, B, S, H, hd, mode)
+        return y
+    dout = np.empty_like(out)
+    dlse = np.empty_like(lse)
+    lib().orc_ctx_scale(_p(out), _p(lse), _p(ln_pad), _p(u16(dy)), None, _p(dout), _p(dlse), B, S, H,
+                        hd, mode)
+    return dout, dlse

@@ -227,6 +227,66 @@ float orc_exp_nonpos(float a) {
   return (p * ldexpf(1.0f, ki + 64)) * ldexpf(1.0f, -64);
 }
 
+/* exp(a) for every fp32 a: the reduction and polynomial of orc_exp_nonpos
+ * (identical for a <= 0), two-step scaling above 2^127, overflow to infinity
+ * beyond exp's range, NaN propagated.  Mirrors canonical_exp of the device. */
+float orc_exp(float a) {
+  if (a != a) return a + a;
+  if (a < -104.0f) return 0.0f;
+  if (a > 88.8f) return INFINITY;
+  const float k = rintf(a * 1.44269502162933349609375f);
+  float r = fmaf(k, -0.693145751953125f, a);
+  r = fmaf(k, -1.428606765330187e-06f, r);
+  float p = 1.98412701138295233249664306640625e-04f;
+  p = fmaf(p, r, 1.38888892251998186111450195312500e-03f);
+  p = fmaf(p, r, 8.33333376795053482055664062500000e-03f);
+  p = fmaf(p, r, 4.16666679084300994873046875000000e-02f);
+  p = fmaf(p, r, 1.66666671633720397949218750000000e-01f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const int ki = (int)k;
+  if (ki > 127) return (p * ldexpf(1.0f, 64)) * ldexpf(1.0f, ki - 64);
+  if (ki >= -125) return p * ldexpf(1.0f, ki);
+  return (p * ldexpf(1.0f, ki + 64)) * ldexpf(1.0f, -64);
+}
+
+/* src/kernels/ctx_scale.py:8-37 and :61-100.  Per token s of batch b and head
+ * h: gain = 1 / (1 + exp(ln_pad[b] - lse[b,h,s])); y = bf16(x * gain).
+ * Backward: dout = bf16(dy * gain); dlse = (sum(dy * x) * gain) * (1 - gain),
+ * the sum over the head's hd elements in canonical order (P = hd/8), or the
+ * numpy order in INTERP mode.  out/dy/y/dout [B,S,H,hd] bf16, lse/dlse
+ * [B,H,S] fp32, ln_pad [B] fp32.  In INTERP mode exp is the C library's expf,
+ * standing in for the interpreter's numpy exp (last-bit differences remain). */
+void orc_ctx_scale(const uint16_t* out, const float* lse, const float* ln_pad, const uint16_t* dy,
+                   uint16_t* y, uint16_t* dout, float* dlse, int64_t B, int64_t S, int64_t H,
+                   int64_t hd, int mode) {
+  float* t = (float*)malloc((size_t)hd * sizeof(float));
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t s = 0; s < S; ++s)
+      for (int64_t h = 0; h < H; ++h) {
+        const int64_t li = (b * H + h) * S + s;
+        const float a = ln_pad[b] - lse[li];
+        const float e = mode == ROUND_INTERP ? expf(a) : orc_exp(a);
+        const float gain = 1.0f / (1.0f + e);
+        const int64_t o = ((b * S + s) * H + h) * hd;
+        for (int64_t i = 0; i < hd; ++i) {
+          const float x = orc_bf16_to_f32(out[o + i]);
+          if (y) y[o + i] = orc_f32_to_bf16(x * gain, mode);
+          if (dy) {
+            const float g = orc_bf16_to_f32(dy[o + i]);
+            dout[o + i] = orc_f32_to_bf16(g * gain, mode);
+            t[i] = g * x;
+          }
+        }
+        if (dy) {
+          const float sum = mode == ROUND_INTERP ? orc_numpy_sum(t, hd) : orc_canonical_sum(t, hd, (int)(hd / 8));
+          dlse[li] = (sum * gain) * (1.0f - gain);
+        }
+      }
+  free(t);
+}
+
 /* GELU with the Abramowitz & Stegun 7.1.26 erf (src/kernels/fp8.py:260-270),
  * Horner steps as fmaf. */
 float orc_gelu(float x) {

@@ -44,6 +44,7 @@ def main() -> None:
     import torch
     import triton
     from src.kernels import adaln as A
+    from src.kernels import ctx_scale as CS
     from src.kernels import fp8 as F8
     from src.kernels import rope as R
     from src.model import rope_tables
@@ -207,6 +208,22 @@ def main() -> None:
     y = torch.empty(B, S, H, hd, dtype=bf)
     R._head_norm_kernel.fn[(B * S, triton.cdiv(H, 2))](x, y, w, 1e-5, HEADS=H, HALF=hd // 2, HPP=2)
     save("head_norm_h4", x=x, w=w, y=y, heads=np.int64(H), eps=np.float32(1e-5))
+
+    # ctx_scale forward and backward (src/kernels/ctx_scale.py:8-37, :61-100).
+    # lse spreads over saturated gains on both sides.
+    for (B, S, H, hd) in ((2, 5, 4, 128), (1, 3, 5, 64)):
+        out = randn(B, S, H, hd).to(bf)
+        lse = randn(B, H, S, std=4.0) + 2.0
+        ln_pad = torch.tensor([0.5, 4.0][:B], dtype=torch.float32)
+        dy = randn(B, S, H, hd, std=1e-2).to(bf)
+        block = triton.next_power_of_2(H)
+        y = torch.empty_like(out)
+        CS._ctx_scale_kernel[(B * S,)](out, lse, ln_pad, y, S, HEADS=H, HD=hd, BLOCK_H=block)
+        dout = torch.empty_like(out)
+        dlse = torch.empty_like(lse)
+        CS._ctx_scale_bwd_kernel[(B * S,)](out, lse, ln_pad, dy, dout, dlse, S, HEADS=H, HD=hd,
+                                              BLOCK_H=block)
+        save(f"ctx_scale_h{H}_d{hd}", out=out, lse=lse, ln_pad=ln_pad, dy=dy, y=y, dout=dout, dlse=dlse)
 
 
 if __name__ == "__main__":

@@ -82,6 +82,16 @@ def test_rejects_bad_head_dim_and_K():
     assert rc == 1 and "K must be" in msg
 
 
+def test_ctx_scale_rejects_bad_shapes():
+    rc, msg = _status("afb_ctx_scale", FAKE, FAKE, FAKE, FAKE, 1, 4, 16, 96, None)
+    assert rc == 1 and "afb_ctx_scale" in msg and "head_dim" in msg
+    rc, msg = _status("afb_ctx_scale_bwd", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 4, 32, 128, None)
+    assert rc == 1 and "heads * head_dim" in msg
+    rc, msg = _status("afb_ctx_scale", FAKE, FAKE + 2, FAKE, FAKE, 1, 4, 16, 128, None)
+    assert rc == 1 and "lse is not 4-byte aligned" in msg
+    assert _status("afb_ctx_scale", FAKE, FAKE, FAKE, FAKE, 0, 4, 16, 128, None)[0] == 0
+
+
 def test_empty_inputs_are_a_no_op():
     assert _status("afb_residual_adaln", *([FAKE] * 7), 0, 4, 2048, 1e-6, None)[0] == 0
     assert _status("afb_rowquant", FAKE, FAKE, FAKE, 0, 2048, 1, None)[0] == 0

@@ -276,3 +276,48 @@ def test_formulation_adaln_bwd_matches_autograd():
     assert np.abs(dz - dz_ref.numpy()).max() <= 2 * 2.0 ** -8 * np.abs(dz_ref.numpy()).max()
     dsc = (o["dscale"].astype(np.uint32) << 16).view(np.float32)
     assert np.abs(dsc - sc.grad.numpy()).max() <= 2 * 2.0 ** -8 * np.abs(sc.grad.numpy()).max()
+
+
+@pytest.mark.parametrize("name", ["ctx_scale_h4_d128", "ctx_scale_h5_d64"])
+def test_pin_ctx_scale(name):
+    """INTERP mode against the reference kernels run by the interpreter: the
+    interpreter's exp is numpy's, the oracle's is the C library's, so a gain
+    may differ in its last fp32 bit; after the truncating bf16 cast the
+    outputs then differ by at most one bf16 step, and almost never."""
+    g = golden(name)
+    y = C.ctx_scale(g["out"], g["lse"], g["ln_pad"], mode=C.INTERP)
+    dout, dlse = C.ctx_scale(g["out"], g["lse"], g["ln_pad"], dy=g["dy"], mode=C.INTERP)
+    for ours, ref in ((y, g["y"]), (dout, g["dout"])):
+        step = np.abs(ours.astype(np.int32) - ref.astype(np.int32))
+        assert step.max() <= 1 and (step > 0).mean() < 0.01
+    np.testing.assert_allclose(dlse, g["dlse"], rtol=1e-5, atol=1e-12)
+
+
+def test_canonical_exp_accuracy():
+    """The canonical exp stays within one ulp of the correctly rounded value
+    over exp's normal range, and saturates at both ends."""
+    rng = np.random.default_rng(3)
+    xs = rng.uniform(-87.0, 88.7, 4000).astype(np.float32)
+    for a in xs:
+        e = np.float32(C.exp(float(a)))
+        t = np.float32(np.exp(np.float64(a)))
+        assert abs(float(e) - float(t)) <= float(np.spacing(t))
+    assert C.exp(-200.0) == 0.0 and C.exp(100.0) == float("inf") and np.isnan(C.exp(float("nan")))
+
+
+@pytest.mark.parametrize("name", ["ctx_scale_h4_d128"])
+def test_formulation_ctx_scale(name):
+    """The canonical (RNE) ctx_scale against a float64 evaluation of the
+    reference formula: bf16 outputs within one step, dlse to 1e-5."""
+    g = golden(name)
+    x = (g["out"].astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    dy = (g["dy"].astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    B, S, H, hd = x.shape
+    lse = g["lse"].astype(np.float64).transpose(0, 2, 1)[..., None]  # [B, S, H, 1]
+    gain = 1.0 / (1.0 + np.exp(g["ln_pad"].astype(np.float64)[:, None, None, None] - lse))
+    y = C.ctx_scale(g["out"], g["lse"], g["ln_pad"])
+    dout, dlse = C.ctx_scale(g["out"], g["lse"], g["ln_pad"], dy=g["dy"])
+    yf = (y.astype(np.uint32) << 16).view(np.float32)
+    assert np.all(np.abs(yf - x * gain) <= np.abs(x * gain) * 2.0 ** -7 + 1e-30)
+    ref_dlse = ((dy * x).sum(-1, keepdims=True) * gain * (1.0 - gain))[..., 0].transpose(0, 2, 1)
+    np.testing.assert_allclose(dlse, ref_dlse, rtol=1e-5, atol=1e-10)
