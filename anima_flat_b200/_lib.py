@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple] = {
     "afb_head_norm_bwd": (_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, ctypes.c_size_t, _P),
     "afb_ctx_scale": (_P, _P, _P, _P, _I, _I, _I, _I, _P),
     "afb_ctx_scale_bwd": (_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P),
+    "afb_rms_silu": (_P, _P, _P, _P, _P, _I, _I, _I, _I, c_int, _P),
+    "afb_rms_silu_bwd": (_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, c_int, _P, ctypes.c_size_t, _P),
 }
 
 # Workspace-size queries: name -> argument types (return size_t).
@@ -48,6 +50,7 @@ WORKSPACE_QUERIES: dict[str, tuple] = {
     "afb_adaln_bwd_workspace": (_I, _I, _I),
     "afb_qkv_norm_rope_bwd_workspace": (_I, _I, _I, _I),
     "afb_head_norm_bwd_workspace": (_I, _I, _I, _I),
+    "afb_rms_silu_bwd_workspace": (_I, _I),
 }
 
 _lib: ctypes.CDLL | None = None

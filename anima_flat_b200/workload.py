@@ -95,6 +95,23 @@ def bytes_ctx_scale_bwd(s: Shape) -> int:
     return s.rows * s.heads * s.head_dim * 2 * 3 + s.rows * s.heads * 4 * 2 + s.batch * 4
 
 
+# The VAE decoder's last stage at 1024x1024: 1M pixels of 96 channels.
+VAE_ROWS = 1024 * 1024
+VAE_C = 96
+
+
+def bytes_rms(name: str, rows: int = VAE_ROWS, C: int = VAE_C) -> int:
+    """Algorithmic bytes of the rms_silu family: bf16 activations read and
+    written once, plus gamma (and gamma's gradient)."""
+    t = rows * C * 2
+    return {
+        "rms_silu": 2 * t + C * 4,                 # x in, y out
+        "add_rms_silu": 4 * t + C * 4,             # x, r in; s, y out
+        "shuffle_rms_silu": 3 * t + C * 4,         # u in; s, y out
+        "rms_silu_bwd": 4 * t + 2 * C * 4,         # s, dy, gs in; ds out; gamma in, dgamma out
+    }[name]
+
+
 def bf16_forward_calls(s: Shape) -> list[str]:
     """Op names in call order for forward_fused (model.py:366-375)."""
     calls = ["adaln"]
@@ -134,6 +151,10 @@ def call_bytes(name: str, s: Shape) -> int:
         "head_norm_bwd": bytes_head_norm_bwd,
         "ctx_scale": bytes_ctx_scale,
         "ctx_scale_bwd": bytes_ctx_scale_bwd,
+        "rms_silu": lambda sh: bytes_rms("rms_silu"),
+        "add_rms_silu": lambda sh: bytes_rms("add_rms_silu"),
+        "shuffle_rms_silu": lambda sh: bytes_rms("shuffle_rms_silu"),
+        "rms_silu_bwd": lambda sh: bytes_rms("rms_silu_bwd"),
     }[name](s)
 
 

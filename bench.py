@@ -609,7 +609,8 @@ def run_reference(args, world, rank):
 # ------------------------------------------------------------- per-op table --
 PER_OPS = ["residual_adaln", "adaln", "qkv_norm_rope", "head_norm", "residual_adaln_fp8",
            "adaln_fp8", "rowquant", "rowquant_gelu", "residual_adaln_bwd", "adaln_bwd",
-           "qkv_norm_rope_bwd", "head_norm_bwd", "ctx_scale", "ctx_scale_bwd"]
+           "qkv_norm_rope_bwd", "head_norm_bwd", "ctx_scale", "ctx_scale_bwd", "rms_silu",
+           "add_rms_silu", "shuffle_rms_silu", "rms_silu_bwd"]
 
 
 def run_per_op(args):
@@ -667,6 +668,24 @@ def run_per_op(args):
             ops = torch.ops.anima_flat_b200
             sets = [(act(B, S, H * hd), act(B, S, H, hd) * 0.01, w, H, 1e-5) for _ in range(nbuf)]
             fn = ops.head_norm_bwd
+        elif name in ("rms_silu", "add_rms_silu", "shuffle_rms_silu", "rms_silu_bwd"):
+            # the VAE decoder's last stage at 1024x1024: [1, 1024, 1024, 96]
+            Cv, side = W.VAE_C, 1024
+            gam = 1.0 + 0.1 * torch.randn(Cv, generator=g, device=device)
+            if name == "rms_silu":
+                sets = [(act(1, side, side, Cv), gam) for _ in range(nbuf)]
+                fn = afb.rms_silu
+            elif name == "add_rms_silu":
+                sets = [(act(1, side, side, Cv), act(1, side, side, Cv), gam) for _ in range(nbuf)]
+                fn = afb.add_rms_silu
+            elif name == "shuffle_rms_silu":
+                sets = [(act(1, side // 2, side // 2, 4 * Cv), gam) for _ in range(nbuf)]
+                fn = afb.shuffle_rms_silu
+            else:
+                ops = torch.ops.anima_flat_b200
+                sets = [(act(1, side, side, Cv), gam, act(1, side, side, Cv) * 0.01,
+                         act(1, side, side, Cv) * 0.01, False) for _ in range(nbuf)]
+                fn = ops.rms_silu_bwd
         elif name in ("ctx_scale", "ctx_scale_bwd"):  # cross-attention output at config 2
             lse = lambda: 2.0 + 4.0 * torch.randn(B, H, S, generator=g, device=device)
             lnp = torch.full((B,), 4.0, device=device)
@@ -719,8 +738,10 @@ def run_per_op(args):
             iso = sorted(x.elapsed_time(y) * 1e3 for x, y in ev)
             us_iso = iso[len(iso) // 2]
             del graph
+        shape = ({"batch": 1, "height": 1024, "width": 1024, "channels": W.VAE_C} if "rms_silu" in name
+                 else {"batch": B, "seq": S, "dim": D, "heads": H, "head_dim": hd})
         print(json.dumps({
-            "op": name, "shape": {"batch": B, "seq": S, "dim": D, "heads": H, "head_dim": hd},
+            "op": name, "shape": shape,
             "bytes_per_launch": nbytes, "launches": n, "buffers": nbuf,
             "us_stream": round(us_stream, 3), "gbs_stream": round(nbytes / us_stream / 1e3, 1),
             "frac_stream": round(nbytes / us_stream / 1e3 / peak, 4),

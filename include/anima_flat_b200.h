@@ -126,6 +126,19 @@ int afb_head_norm(const void* x, const void* weight, void* y, int64_t batch,
 int afb_ctx_scale(const void* out, const void* lse, const void* ln_pad, void* y, int64_t batch,
                   int64_t seq, int64_t heads, int64_t head_dim, void* stream);
 
+/* Replaces src/kernels/rms.py:157-197 (anima_flat::rms_silu, add_rms_silu,
+ * shuffle_rms_silu, all launching _fwd_kernel, rms.py:35-73), called from
+ * src/vae.py:74, 258-278.  Rows are pixels of `channels` channels, channels
+ * last, bf16; gamma [channels] fp32.
+ *   rms_silu:         residual NULL, shuffled 0; s unused (may be NULL).
+ *   add_rms_silu:     residual [rows, C]; s = bf16(x + residual) is written.
+ *   shuffle_rms_silu: shuffled 1, x = u [B, H/2, W/2, 4C], output grid
+ *                     H x W (rows = B*H*W); s = the gathered x is written.
+ * y = bf16(silu(s * sqrt(C) / max(|s|, 1e-12) * gamma)).  channels a
+ * multiple of 8 in [8, 1024]. */
+int afb_rms_silu(const void* x, const void* residual, const void* gamma, void* s, void* y,
+                 int64_t rows, int64_t H, int64_t W, int64_t channels, int shuffled, void* stream);
+
 /* ----------------------------------------------------------------------- */
 /* Backward (LoRA training)                                                 */
 /* ----------------------------------------------------------------------- */
@@ -198,6 +211,16 @@ int afb_head_norm_bwd(const void* x, const void* dy, const void* weight, void* d
 int afb_ctx_scale_bwd(const void* out, const void* lse, const void* ln_pad, const void* dy,
                       void* dout, void* dlse, int64_t batch, int64_t seq, int64_t heads,
                       int64_t head_dim, void* stream);
+
+/* Replaces src/kernels/rms.py:200-243 (anima_flat::rms_silu_bwd, launching
+ * _bwd_kernel, rms.py:76-125; partials reduced here in a fixed order instead
+ * of torch .sum).  s [rows, C] (the saved s or x); dy [rows, C]; gs (the
+ * gradient of s for add/shuffle) or NULL; ds in the input layout (u's layout
+ * when shuffled); dgamma [C] fp32.  Workspace from the query. */
+size_t afb_rms_silu_bwd_workspace(int64_t rows, int64_t channels);
+int afb_rms_silu_bwd(const void* s, const void* gamma, const void* dy, const void* gs, void* ds,
+                     void* dgamma, int64_t rows, int64_t H, int64_t W, int64_t channels,
+                     int shuffled, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -37,6 +37,9 @@ def lib():
             "orc_e4m3_to_f32": ([ctypes.c_uint8], c_float),
             "orc_exp": ([c_float], c_float),
             "orc_ctx_scale": ([P] * 7 + [I, I, I, I, N], None),
+            "orc_rms_lpr": ([I], N),
+            "orc_rms_silu_fwd": ([P] * 5 + [I, I, I, I, N, N], None),
+            "orc_rms_silu_bwd": ([P] * 6 + [I, I, I, I, N, N], None),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(L, name)
@@ -213,3 +216,47 @@ def ctx_scale(out, lse, ln_pad, dy=None, mode=RNE):
     lib().orc_ctx_scale(_p(out), _p(lse), _p(ln_pad), _p(u16(dy)), None, _p(dout), _p(dlse), B, S, H,
                         hd, mode)
     return dout, dlse
+
+
+def rms_lpr(C: int) -> int:
+    """Lanes per row of the canonical rms order (P of its row sums)."""
+    return int(lib().orc_rms_lpr(C))
+
+
+def rms_silu_fwd(x, g, r=None, shuffled=False, mode=RNE):
+    """rms_silu (r None, not shuffled): returns y; add_rms_silu (r given) and
+    shuffle_rms_silu (shuffled, x = u [B, h, w, 4C]): return (s, y).
+    Activations are bf16 bits, channels last; g is [C] fp32."""
+    x = u16(x)
+    g = f32(g)
+    C = g.size
+    if shuffled:
+        B, h, w, _ = x.shape
+        shape, H, W = (B, 2 * h, 2 * w, C), 2 * h, 2 * w
+    else:
+        shape, H, W = x.shape, 0, 0
+    N = int(np.prod(shape[:-1]))
+    y = np.empty(shape, np.uint16)
+    s = np.empty(shape, np.uint16) if (r is not None or shuffled) else None
+    lib().orc_rms_silu_fwd(_p(x), _p(u16(r)) if r is not None else None, _p(g), _p(s), _p(y), N, H, W,
+                           C, int(shuffled), mode)
+    return y if s is None else (s, y)
+
+
+def rms_silu_bwd(s, g, dy, gs=None, shuffled=False, mode=RNE):
+    """Returns (ds, dg): ds in the input layout (u's with shuffled), dg [C] fp32."""
+    s = u16(s)
+    g = f32(g)
+    C = g.size
+    if shuffled:
+        B, H, W, _ = s.shape
+        ds_shape = (B, H // 2, W // 2, 4 * C)
+    else:
+        H = W = 0
+        ds_shape = s.shape
+    N = int(np.prod(s.shape[:-1]))
+    ds = np.empty(ds_shape, np.uint16)
+    dg = np.empty(C, np.float32)
+    lib().orc_rms_silu_bwd(_p(s), _p(g), _p(u16(dy)), _p(u16(gs)) if gs is not None else None, _p(ds),
+                           _p(dg), N, H, W, C, int(shuffled), mode)
+    return ds, dg

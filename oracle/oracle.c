@@ -251,6 +251,125 @@ float orc_exp(float a) {
   return (p * ldexpf(1.0f, ki + 64)) * ldexpf(1.0f, -64);
 }
 
+static void stride_tree_rows(const float* rows, int64_t n, int64_t cols, float* out);
+
+/* Channel RMS norm + SiLU of the VAE (src/kernels/rms.py:20-123).  Rows are
+ * pixels of C channels (channels last).  Lanes per row in the canonical
+ * order: LPR = the smallest power of two with at most four 8-element vectors
+ * per lane, at most 32; row sums are canonical sums with P = LPR. */
+int orc_rms_lpr(int64_t C) {
+  const int64_t nv = C / 8;
+  int lpr = 1;
+  while (lpr < 32 && (int64_t)lpr * 4 < nv) lpr <<= 1;
+  return lpr;
+}
+
+/* Source offset of output row `row` (rms.py:20-32): with `shuf`, output pixel
+ * (b, y, x) of an [B, H, W, C] grid reads the sub-pixel channels of
+ * u[b, y/2, x/2, ((y%2)*2 + x%2)*C + c]. */
+static int64_t rms_src(int64_t row, int64_t H, int64_t W, int64_t C, int shuf) {
+  if (!shuf) return row * C;
+  const int64_t hw = H * W, b = row / hw, rem = row - b * hw, y = rem / W, x = rem - y * W;
+  return (((b * (H / 2) + y / 2) * (W / 2) + x / 2) * 4 + (y % 2) * 2 + x % 2) * C;
+}
+
+static float rms_sigmoid(float a, int mode) {
+  const float e = mode == ROUND_INTERP ? expf(-a) : orc_exp(-a);
+  return 1.0f / (1.0f + e);
+}
+
+/* Forward (rms.py:35-73): s = bf16(x + r) with r, the gathered x with shuf,
+ * else x; rstd = sqrt(C) / max(sqrt(sum(s^2)), 1e-12); a = (s * rstd) * g;
+ * y = bf16(a * sigmoid(a)).  s_out (when given) receives s. */
+void orc_rms_silu_fwd(const uint16_t* x, const uint16_t* r, const float* g, uint16_t* s_out,
+                      uint16_t* y, int64_t N, int64_t H, int64_t W, int64_t C, int shuf, int mode) {
+  float* sv = (float*)malloc((size_t)C * sizeof(float));
+  float* t = (float*)malloc((size_t)C * sizeof(float));
+  const int P = orc_rms_lpr(C);
+  const float sqrt_c = (float)sqrt((double)C);
+  for (int64_t row = 0; row < N; ++row) {
+    const int64_t src = rms_src(row, H, W, C, shuf), dst = row * C;
+    for (int64_t c = 0; c < C; ++c) {
+      float v = orc_bf16_to_f32(x[src + c]);
+      if (r) v = orc_bf16_to_f32(orc_f32_to_bf16(v + orc_bf16_to_f32(r[dst + c]), mode));
+      sv[c] = v;
+      if (s_out) s_out[dst + c] = orc_f32_to_bf16(v, mode);
+      t[c] = v * v;
+    }
+    const float ss = mode == ROUND_INTERP ? orc_numpy_sum(t, C) : orc_canonical_sum(t, C, P);
+    const float nrm = sqrtf(ss);
+    const float rstd = sqrt_c / (nrm > 1e-12f ? nrm : 1e-12f);
+    for (int64_t c = 0; c < C; ++c) {
+      const float a = (sv[c] * rstd) * g[c];
+      y[dst + c] = orc_f32_to_bf16(a * rms_sigmoid(a, mode), mode);
+    }
+  }
+  free(sv);
+  free(t);
+}
+
+/* Backward (rms.py:76-125): per row, rstd of s as the forward; n = s * rstd;
+ * a = n * g; sg = sigmoid(a); da = (dy * sg) * (1 + a * (1 - sg));
+ * dn = da * g; ds = rstd * (dn - n * (sum(dn * n) / C)) (+ gs), stored at the
+ * source offset; dg = sum over rows of da * n.  dg order: tiles of 32/P rows
+ * (a stride tree over the tile's rows), 32 tiles per chunk summed in order
+ * from zero, chunks by a stride tree. */
+void orc_rms_silu_bwd(const uint16_t* s, const float* g, const uint16_t* dy, const uint16_t* gs,
+                      uint16_t* ds, float* dg, int64_t N, int64_t H, int64_t W, int64_t C, int shuf,
+                      int mode) {
+  const int P = orc_rms_lpr(C);
+  const int T = 32 / P;                      /* rows per tile */
+  const int64_t chunk_rows = (int64_t)T * 32; /* 32 tiles per chunk */
+  const int64_t chunks = (N + chunk_rows - 1) / chunk_rows;
+  const float sqrt_c = (float)sqrt((double)C);
+  float* n = (float*)malloc((size_t)C * sizeof(float));
+  float* da = (float*)malloc((size_t)C * sizeof(float));
+  float* t = (float*)malloc((size_t)C * sizeof(float));
+  float* tile = (float*)malloc((size_t)T * C * sizeof(float));
+  float* cs = (float*)malloc((size_t)(chunks > 0 ? chunks : 1) * C * sizeof(float));
+  for (int64_t ch = 0; ch < chunks; ++ch) {
+    float* acc = cs + ch * C;
+    for (int64_t c = 0; c < C; ++c) acc[c] = 0.0f;
+    for (int tl = 0; tl < 32; ++tl) {
+      for (int64_t i = 0; i < (int64_t)T * C; ++i) tile[i] = 0.0f;
+      for (int k = 0; k < T; ++k) {
+        const int64_t row = ch * chunk_rows + (int64_t)tl * T + k;
+        if (row >= N) continue;
+        const int64_t dst = row * C;
+        for (int64_t c = 0; c < C; ++c) {
+          const float v = orc_bf16_to_f32(s[dst + c]);
+          t[c] = v * v;
+        }
+        const float ss = mode == ROUND_INTERP ? orc_numpy_sum(t, C) : orc_canonical_sum(t, C, P);
+        const float nrm = sqrtf(ss);
+        const float rstd = sqrt_c / (nrm > 1e-12f ? nrm : 1e-12f);
+        for (int64_t c = 0; c < C; ++c) {
+          n[c] = orc_bf16_to_f32(s[dst + c]) * rstd;
+          const float a = n[c] * g[c];
+          const float sg = rms_sigmoid(a, mode);
+          da[c] = (orc_bf16_to_f32(dy[dst + c]) * sg) * (1.0f + a * (1.0f - sg));
+          tile[(int64_t)k * C + c] = da[c] * n[c];
+          t[c] = (da[c] * g[c]) * n[c];
+        }
+        const float sdn = mode == ROUND_INTERP ? orc_numpy_sum(t, C) : orc_canonical_sum(t, C, P);
+        const float m = sdn / (float)C;
+        const int64_t src = rms_src(row, H, W, C, shuf);
+        for (int64_t c = 0; c < C; ++c) {
+          float v = rstd * (da[c] * g[c] - n[c] * m);
+          if (gs) v = v + orc_bf16_to_f32(gs[dst + c]);
+          ds[src + c] = orc_f32_to_bf16(v, mode);
+        }
+      }
+      for (int w = T; w > 1; w /= 2) /* stride tree over the tile's rows */
+        for (int k = 0; k < w / 2; ++k)
+          for (int64_t c = 0; c < C; ++c) tile[(int64_t)k * C + c] = tile[(int64_t)k * C + c] + tile[(int64_t)(k + w / 2) * C + c];
+      for (int64_t c = 0; c < C; ++c) acc[c] = acc[c] + tile[c];
+    }
+  }
+  stride_tree_rows(cs, chunks, C, dg);
+  free(n); free(da); free(t); free(tile); free(cs);
+}
+
 /* src/kernels/ctx_scale.py:8-37 and :61-100.  Per token s of batch b and head
  * h: gain = 1 / (1 + exp(ln_pad[b] - lse[b,h,s])); y = bf16(x * gain).
  * Backward: dout = bf16(dy * gain); dlse = (sum(dy * x) * gain) * (1 - gain),

@@ -45,6 +45,7 @@ def main() -> None:
     import triton
     from src.kernels import adaln as A
     from src.kernels import ctx_scale as CS
+    from src.kernels import rms as RM
     from src.kernels import fp8 as F8
     from src.kernels import rope as R
     from src.model import rope_tables
@@ -224,6 +225,44 @@ def main() -> None:
         CS._ctx_scale_bwd_kernel[(B * S,)](out, lse, ln_pad, dy, dout, dlse, S, HEADS=H, HD=hd,
                                               BLOCK_H=block)
         save(f"ctx_scale_h{H}_d{hd}", out=out, lse=lse, ln_pad=ln_pad, dy=dy, y=y, dout=dout, dlse=dlse)
+
+    # VAE rms_silu family (src/kernels/rms.py:35-125), launched through the
+    # autotuner's JITFunction with a fixed tile: R = 1 row per step, ROWS = 8
+    # rows per backward chunk.
+    for name, (shape, C, add, shuf) in {
+        "rms_silu_c96": ((1, 4, 6, 96), 96, False, False),
+        "add_rms_silu_c192": ((2, 3, 5, 192), 192, True, False),
+        "shuffle_rms_silu_c96": ((1, 2, 3, 384), 96, False, True),
+    }.items():
+        x = randn(*shape).to(bf)
+        r = randn(*shape).to(bf) if add else None
+        g = 1.0 + randn(C, std=0.1)
+        if shuf:
+            B, h, w, _ = shape
+            oshape, H, W = (B, 2 * h, 2 * w, C), 2 * h, 2 * w
+        else:
+            oshape, H, W = shape, 0, 0
+        N = int(np.prod(oshape[:-1]))
+        y = torch.empty(oshape, dtype=bf)
+        s = torch.empty(oshape, dtype=bf) if (add or shuf) else x
+        RM._fwd_kernel.fn[(N,)](x, r if r is not None else x, g, s, y, N, H, W, C=C,
+                                BLOCK=triton.next_power_of_2(C), HAS_R=add, SHUF=shuf, R=1)
+        dy = randn(*oshape, std=1e-2).to(bf)
+        gs = randn(*oshape, std=1e-2).to(bf) if (add or shuf) else None
+        rows = 8
+        chunks = triton.cdiv(N, rows)
+        ds = torch.empty(x.shape, dtype=bf)
+        pg = torch.empty(chunks, C, dtype=torch.float32)
+        RM._bwd_kernel.fn[(chunks,)](s, g, dy, gs if gs is not None else dy, ds, pg, N, H, W, C=C,
+                                     BLOCK=triton.next_power_of_2(C), ROWS=rows, HAS_GS=gs is not None,
+                                     SHUF=shuf, R=1)
+        arrays = dict(x=x, g=g, y=y, dy=dy, ds=ds, dg=pg.sum(0))
+        if r is not None:
+            arrays["r"] = r
+        if add or shuf:
+            arrays["s"] = s
+            arrays["gs"] = gs
+        save(name, **arrays)
 
 
 if __name__ == "__main__":

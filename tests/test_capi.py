@@ -92,6 +92,20 @@ def test_ctx_scale_rejects_bad_shapes():
     assert _status("afb_ctx_scale", FAKE, FAKE, FAKE, FAKE, 0, 4, 16, 128, None)[0] == 0
 
 
+def test_rms_silu_rejects_bad_channels_and_grid():
+    rc, msg = _status("afb_rms_silu", FAKE, None, FAKE, None, FAKE, 4, 0, 0, 100, 0, None)
+    assert rc == 1 and "afb_rms_silu" in msg and "multiple of 8" in msg
+    rc, msg = _status("afb_rms_silu", FAKE, None, FAKE, FAKE, FAKE, 12, 3, 4, 96, 1, None)
+    assert rc == 1 and "even output grid" in msg
+    assert lib_ws("afb_rms_silu_bwd_workspace", 1024 * 1024, 96) == (1024 * 1024 // 256) * 96 * 4
+    rc, msg = _status("afb_rms_silu_bwd", FAKE, FAKE, FAKE, None, FAKE, FAKE, 4096, 0, 0, 96, 0, FAKE, 16, None)
+    assert rc == 1 and "workspace too small" in msg
+
+
+def lib_ws(name, *args):
+    return int(getattr(_lib.load(), name)(*args))
+
+
 def test_empty_inputs_are_a_no_op():
     assert _status("afb_residual_adaln", *([FAKE] * 7), 0, 4, 2048, 1e-6, None)[0] == 0
     assert _status("afb_rowquant", FAKE, FAKE, FAKE, 0, 2048, 1, None)[0] == 0

@@ -321,3 +321,24 @@ def test_formulation_ctx_scale(name):
     assert np.all(np.abs(yf - x * gain) <= np.abs(x * gain) * 2.0 ** -7 + 1e-30)
     ref_dlse = ((dy * x).sum(-1, keepdims=True) * gain * (1.0 - gain))[..., 0].transpose(0, 2, 1)
     np.testing.assert_allclose(dlse, ref_dlse, rtol=1e-5, atol=1e-10)
+
+
+@pytest.mark.parametrize("name,shuffled", [("rms_silu_c96", False), ("add_rms_silu_c192", False),
+                                           ("shuffle_rms_silu_c96", True)])
+def test_pin_rms_silu(name, shuffled):
+    """INTERP mode reproduces the reference's VAE kernels bit for bit (s, y,
+    ds); the gamma gradient, summed in another order, agrees to 1e-5."""
+    g = golden(name)
+    out = C.rms_silu_fwd(g["x"], g["g"], r=g.get("r"), shuffled=shuffled, mode=C.INTERP)
+    if isinstance(out, tuple):
+        np.testing.assert_array_equal(out[0], g["s"])
+        out = out[1]
+    np.testing.assert_array_equal(out, g["y"])
+    ds, dg = C.rms_silu_bwd(g.get("s", g["x"]), g["g"], g["dy"], gs=g.get("gs"), shuffled=shuffled,
+                            mode=C.INTERP)
+    np.testing.assert_array_equal(ds, g["ds"])
+    np.testing.assert_allclose(dg, g["dg"], rtol=1e-5)
+
+
+def test_rms_lanes_per_row():
+    assert [C.rms_lpr(c) for c in (8, 32, 40, 96, 192, 384, 768, 1024)] == [1, 1, 2, 4, 8, 16, 32, 32]
