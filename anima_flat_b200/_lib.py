@@ -28,6 +28,7 @@ SIGNATURES: dict[str, tuple] = {
     "afb_adaln_fp8": (_P, _P, _P, _P, _P, _I, _I, _I, _F, _P),
     "afb_rowquant": (_P, _P, _P, _I, _I, c_int, _P),
     "afb_gelu_probe": (_P, _P, _P, _I, _P),
+    "afb_silu_probe": (_P, _P),
     "afb_qkv_norm_rope": (_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P),
     "afb_head_norm": (_P, _P, _P, _I, _I, _I, _I, _F, _P),
     "afb_residual_adaln_bwd": (_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _P,

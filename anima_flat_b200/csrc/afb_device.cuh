@@ -537,7 +537,25 @@ __device__ __forceinline__ float canonical_exp_nonpos(float a) {
 // canonical_exp_nonpos (identical results for a <= 0).  Above 2^127 the scale
 // is applied in two exact steps; beyond exp's range the product overflows to
 // infinity as IEEE multiplication does; NaN propagates.
+//
+// For |a| <= 87 the scale 2^k (|k| <= 126) is a normal number and one product
+// applies it; at k = -126 that equals the two-step scaling below (its first
+// step is exact), so the short path changes no result.
 __device__ __forceinline__ float canonical_exp(float a) {
+  if (fabsf(a) <= 87.0f) {
+    const float k = rintf(__fmul_rn(a, 1.44269502162933349609375f));
+    float r = __fmaf_rn(k, -0.693145751953125f, a);
+    r = __fmaf_rn(k, -1.428606765330187e-06f, r);
+    float p = 1.98412701138295233249664306640625e-04f;
+    p = __fmaf_rn(p, r, 1.38888892251998186111450195312500e-03f);
+    p = __fmaf_rn(p, r, 8.33333376795053482055664062500000e-03f);
+    p = __fmaf_rn(p, r, 4.16666679084300994873046875000000e-02f);
+    p = __fmaf_rn(p, r, 1.66666671633720397949218750000000e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    return __fmul_rn(p, __int_as_float((static_cast<int>(k) + 127) << 23));
+  }
   if (a != a) return a + a;
   if (a < -104.0f) return 0.0f;
   if (a > 88.8f) return __int_as_float(0x7f800000);
@@ -626,6 +644,44 @@ __device__ __forceinline__ f2_t fast_gelu2(f2_t x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(f2hi(arg)));
   const f2_t y = fma2(p ^ kSign, f2(e0, e1), splat2(1.0f));  // 1 - p*e
   return mul2(x, fma2(splat2(0.5f), (y & kAbs) | (x & kSign), splat2(0.5f)));  // copysign(y, x)
+}
+
+// silu(a) = a * sigmoid(a) with sigmoid(a) = RN(1 / RN(1 + canonical_exp(-a))),
+// every step an IEEE fp32 operation (the VAE's rms_silu, src/kernels/rms.py:74).
+// 1/d correctly rounded is the same number whether formed by division or by
+// the correctly rounded reciprocal.
+__device__ __forceinline__ float canonical_sigmoid(float a) {
+  return __frcp_rn(__fadd_rn(1.0f, canonical_exp(-a)));
+}
+__device__ __forceinline__ float canonical_silu(float a) { return __fmul_rn(a, canonical_sigmoid(a)); }
+
+// silu on the special-function unit (ex2.approx, rcp.approx) for a pair of
+// elements.  No product feeds an addition, so the packed operations round
+// lane by lane like their scalar forms and no contraction can change them.
+__device__ __forceinline__ f2_t fast_silu2(f2_t a) {
+  const f2_t t = mul2(a, splat2(-1.44269502162933349609375f));
+  float e0, e1, r0, r1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(f2lo(t)));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(f2hi(t)));
+  const f2_t d = add2(f2(e0, e1), splat2(1.0f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(f2lo(d)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(f2hi(d)));
+  return mul2(a, f2(r0, r1));
+}
+
+// True when bf16(v), v = fast_silu2's value for a, is certainly the bf16
+// rounding of canonical_silu(a): |a| within the fast range and v's low 16 bits
+// more than kSiluMargin steps from the bf16 rounding midpoint 0x8000.  Within
+// the range the two fp32 values lie fewer than kSiluMargin steps apart, so
+// both round to the same bf16 (an exhaustive check over every fp32 a, on the
+// device, tests exactly this implication).  Outside the range (large |a|,
+// where ex2's argument rounding grows, and where 1 + e overflows) and near
+// a midpoint the caller recomputes canonical_silu.
+constexpr float kSiluFastRange = 8.0f;
+constexpr uint32_t kSiluMargin = 32;
+__device__ __forceinline__ bool silu_settled(float a, float v) {
+  const uint32_t d = (__float_as_uint(v) & 0xffffu) - (0x8000u - kSiluMargin);
+  return fabsf(a) <= kSiluFastRange && d > 2u * kSiluMargin;
 }
 
 }  // namespace afb

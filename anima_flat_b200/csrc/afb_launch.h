@@ -40,6 +40,7 @@ cudaError_t read_status_adaln_fwd(int* status);
 cudaError_t read_status_headnorm_fwd(int* status);
 cudaError_t read_status_headnorm_bwd(int* status);
 cudaError_t read_status_adaln_bwd(int* status);
+cudaError_t read_status_rms(int* status);
 
 // Column sums of chunk partials part[batch][n][ncols] (fp32) by a stride tree
 // over the chunk index (finalize.cu); column c goes to out[c / seg][b*seg +

@@ -85,6 +85,10 @@ extern "C" int afb_device_status(int* status) {
     e = afb::read_status_adaln_bwd(&v);
     all |= v;
   }
+  if (e == cudaSuccess) {
+    e = afb::read_status_rms(&v);
+    all |= v;
+  }
   if (e != cudaSuccess) {
     afb::set_error(std::string("afb_device_status: ") + cudaGetErrorString(e));
     return static_cast<int>(e);

@@ -31,6 +31,13 @@ def _validate(x: torch.Tensor, gamma: torch.Tensor, channels: int) -> None:
         raise ValueError(f"gamma must have {channels} elements, got {gamma.numel()}")
 
 
+def _gamma32(gamma: torch.Tensor) -> torch.Tensor:
+    """gamma as a contiguous fp32 array on a 16-byte boundary (the kernels
+    read it in 16-byte vectors)."""
+    g32 = gamma.float().contiguous()
+    return g32 if g32.data_ptr() % 16 == 0 else g32.clone()
+
+
 def _fwd(x, r, gamma, shuffled):
     C = gamma.numel()
     if shuffled:
@@ -43,7 +50,7 @@ def _fwd(x, r, gamma, shuffled):
         rows *= d
     y = x.new_empty(shape)
     s = x.new_empty(shape) if (r is not None or shuffled) else None
-    g32 = gamma.float().contiguous()
+    g32 = _gamma32(gamma)
     call("afb_rms_silu", x.data_ptr(), r.data_ptr() if r is not None else None, g32.data_ptr(),
          s.data_ptr() if s is not None else None, y.data_ptr(), rows, H, W, C, int(shuffled), _stream(x))
     return s, y
@@ -107,7 +114,7 @@ def _rms_silu_bwd(
     ds = s.new_empty(ds_shape)
     dg = torch.empty(C, dtype=torch.float32, device=s.device)
     ws, nbytes = workspace("afb_rms_silu_bwd", s.device, rows, C)
-    g32 = gamma.float().contiguous()
+    g32 = _gamma32(gamma)
     call("afb_rms_silu_bwd", s.data_ptr(), g32.data_ptr(), dy.data_ptr(),
          gs.data_ptr() if gs is not None else None, ds.data_ptr(), dg.data_ptr(), rows, H, W, C,
          int(shuffled), ws.data_ptr(), nbytes, _stream(s))

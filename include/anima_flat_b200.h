@@ -129,15 +129,23 @@ int afb_ctx_scale(const void* out, const void* lse, const void* ln_pad, void* y,
 /* Replaces src/kernels/rms.py:157-197 (anima_flat::rms_silu, add_rms_silu,
  * shuffle_rms_silu, all launching _fwd_kernel, rms.py:35-73), called from
  * src/vae.py:74, 258-278.  Rows are pixels of `channels` channels, channels
- * last, bf16; gamma [channels] fp32.
+ * last, bf16; gamma [channels] fp32, 16-byte aligned like every array.
  *   rms_silu:         residual NULL, shuffled 0; s unused (may be NULL).
  *   add_rms_silu:     residual [rows, C]; s = bf16(x + residual) is written.
  *   shuffle_rms_silu: shuffled 1, x = u [B, H/2, W/2, 4C], output grid
  *                     H x W (rows = B*H*W); s = the gathered x is written.
  * y = bf16(silu(s * sqrt(C) / max(|s|, 1e-12) * gamma)).  channels a
- * multiple of 8 in [8, 1024]. */
+ * multiple of 8 in [8, 1024]; W <= 2^30 when shuffled. */
 int afb_rms_silu(const void* x, const void* residual, const void* gamma, void* s, void* y,
                  int64_t rows, int64_t H, int64_t W, int64_t channels, int shuffled, void* stream);
+
+/* Test hook: every fp32 input through the forward's fast SiLU and its
+ * settle test against the canonical SiLU.  stats: 514 uint64 counters,
+ * 8-byte aligned, overwritten: [0] settled inputs whose bf16 result differs
+ * from the canonical one (0 when the fast path is sound), [1] unsettled
+ * inputs with |a| <= 8, [2 + sign*256 + exponent] the largest fp32-step
+ * distance between the fast and canonical values.  No reference counterpart. */
+int afb_silu_probe(void* stats, void* stream);
 
 /* ----------------------------------------------------------------------- */
 /* Backward (LoRA training)                                                 */
@@ -216,7 +224,10 @@ int afb_ctx_scale_bwd(const void* out, const void* lse, const void* ln_pad, cons
  * _bwd_kernel, rms.py:76-125; partials reduced here in a fixed order instead
  * of torch .sum).  s [rows, C] (the saved s or x); dy [rows, C]; gs (the
  * gradient of s for add/shuffle) or NULL; ds in the input layout (u's layout
- * when shuffled); dgamma [C] fp32.  Workspace from the query. */
+ * when shuffled); dgamma [C] fp32.  Workspace from the query: C floats per
+ * chunk of 8 * 32/L rows (L the lanes per row, the smallest power of two
+ * with C <= 32 * L, at most 32), the chunk doubled until at most 32768
+ * chunks remain. */
 size_t afb_rms_silu_bwd_workspace(int64_t rows, int64_t channels);
 int afb_rms_silu_bwd(const void* s, const void* gamma, const void* dy, const void* gs, void* ds,
                      void* dgamma, int64_t rows, int64_t H, int64_t W, int64_t channels,

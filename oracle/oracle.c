@@ -311,15 +311,26 @@ void orc_rms_silu_fwd(const uint16_t* x, const uint16_t* r, const float* g, uint
 /* Backward (rms.py:76-125): per row, rstd of s as the forward; n = s * rstd;
  * a = n * g; sg = sigmoid(a); da = (dy * sg) * (1 + a * (1 - sg));
  * dn = da * g; ds = rstd * (dn - n * (sum(dn * n) / C)) (+ gs), stored at the
- * source offset; dg = sum over rows of da * n.  dg order: tiles of 32/P rows
- * (a stride tree over the tile's rows), 32 tiles per chunk summed in order
- * from zero, chunks by a stride tree. */
+ * source offset; dg = sum over rows of da * n.  dg order: chunks of TPC tiles
+ * of T = 32/P rows (TPC = 8, doubled until at most 32768 chunks remain);
+ * within a chunk each row group (row index mod T) sums its rows in order
+ * from zero, the T group sums go through a stride tree, the chunk partials
+ * through a stride tree. */
+int orc_rms_tiles_per_chunk(int64_t N, int64_t C) {
+  const int64_t T = 32 / orc_rms_lpr(C);
+  int tpc = 8;
+  while ((N + tpc * T - 1) / (tpc * T) > 32768) tpc <<= 1;
+  return tpc;
+}
+
+
 void orc_rms_silu_bwd(const uint16_t* s, const float* g, const uint16_t* dy, const uint16_t* gs,
                       uint16_t* ds, float* dg, int64_t N, int64_t H, int64_t W, int64_t C, int shuf,
                       int mode) {
   const int P = orc_rms_lpr(C);
   const int T = 32 / P;                      /* rows per tile */
-  const int64_t chunk_rows = (int64_t)T * 32; /* 32 tiles per chunk */
+  const int tpc = orc_rms_tiles_per_chunk(N, C);
+  const int64_t chunk_rows = (int64_t)T * tpc;
   const int64_t chunks = (N + chunk_rows - 1) / chunk_rows;
   const float sqrt_c = (float)sqrt((double)C);
   float* n = (float*)malloc((size_t)C * sizeof(float));
@@ -328,10 +339,8 @@ void orc_rms_silu_bwd(const uint16_t* s, const float* g, const uint16_t* dy, con
   float* tile = (float*)malloc((size_t)T * C * sizeof(float));
   float* cs = (float*)malloc((size_t)(chunks > 0 ? chunks : 1) * C * sizeof(float));
   for (int64_t ch = 0; ch < chunks; ++ch) {
-    float* acc = cs + ch * C;
-    for (int64_t c = 0; c < C; ++c) acc[c] = 0.0f;
-    for (int tl = 0; tl < 32; ++tl) {
-      for (int64_t i = 0; i < (int64_t)T * C; ++i) tile[i] = 0.0f;
+    for (int64_t i = 0; i < (int64_t)T * C; ++i) tile[i] = 0.0f; /* row-group sums */
+    for (int tl = 0; tl < tpc; ++tl) {
       for (int k = 0; k < T; ++k) {
         const int64_t row = ch * chunk_rows + (int64_t)tl * T + k;
         if (row >= N) continue;
@@ -348,7 +357,7 @@ void orc_rms_silu_bwd(const uint16_t* s, const float* g, const uint16_t* dy, con
           const float a = n[c] * g[c];
           const float sg = rms_sigmoid(a, mode);
           da[c] = (orc_bf16_to_f32(dy[dst + c]) * sg) * (1.0f + a * (1.0f - sg));
-          tile[(int64_t)k * C + c] = da[c] * n[c];
+          tile[(int64_t)k * C + c] = tile[(int64_t)k * C + c] + da[c] * n[c];
           t[c] = (da[c] * g[c]) * n[c];
         }
         const float sdn = mode == ROUND_INTERP ? orc_numpy_sum(t, C) : orc_canonical_sum(t, C, P);
@@ -360,11 +369,11 @@ void orc_rms_silu_bwd(const uint16_t* s, const float* g, const uint16_t* dy, con
           ds[src + c] = orc_f32_to_bf16(v, mode);
         }
       }
-      for (int w = T; w > 1; w /= 2) /* stride tree over the tile's rows */
-        for (int k = 0; k < w / 2; ++k)
-          for (int64_t c = 0; c < C; ++c) tile[(int64_t)k * C + c] = tile[(int64_t)k * C + c] + tile[(int64_t)(k + w / 2) * C + c];
-      for (int64_t c = 0; c < C; ++c) acc[c] = acc[c] + tile[c];
     }
+    for (int w = T; w > 1; w /= 2) /* stride tree over the row groups */
+      for (int k = 0; k < w / 2; ++k)
+        for (int64_t c = 0; c < C; ++c) tile[(int64_t)k * C + c] = tile[(int64_t)k * C + c] + tile[(int64_t)(k + w / 2) * C + c];
+    for (int64_t c = 0; c < C; ++c) cs[ch * C + c] = tile[c];
   }
   stride_tree_rows(cs, chunks, C, dg);
   free(n); free(da); free(t); free(tile); free(cs);

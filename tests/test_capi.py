@@ -97,7 +97,10 @@ def test_rms_silu_rejects_bad_channels_and_grid():
     assert rc == 1 and "afb_rms_silu" in msg and "multiple of 8" in msg
     rc, msg = _status("afb_rms_silu", FAKE, None, FAKE, FAKE, FAKE, 12, 3, 4, 96, 1, None)
     assert rc == 1 and "even output grid" in msg
-    assert lib_ws("afb_rms_silu_bwd_workspace", 1024 * 1024, 96) == (1024 * 1024 // 256) * 96 * 4
+    # C = 96: 4 lanes per row, 8 rows per tile, 8 tiles per chunk; the chunk
+    # doubles once 32768 chunks are exceeded
+    assert lib_ws("afb_rms_silu_bwd_workspace", 1024 * 1024, 96) == (1024 * 1024 // 64) * 96 * 4
+    assert lib_ws("afb_rms_silu_bwd_workspace", 4096 * 1024, 96) == (4096 * 1024 // 128) * 96 * 4
     rc, msg = _status("afb_rms_silu_bwd", FAKE, FAKE, FAKE, None, FAKE, FAKE, 4096, 0, 0, 96, 0, FAKE, 16, None)
     assert rc == 1 and "workspace too small" in msg
 
