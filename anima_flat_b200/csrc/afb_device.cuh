@@ -671,17 +671,18 @@ __device__ __forceinline__ f2_t fast_silu2(f2_t a) {
 
 // True when bf16(v), v = fast_silu2's value for a, is certainly the bf16
 // rounding of canonical_silu(a): |a| within the fast range and v's low 16 bits
-// more than kSiluMargin steps from the bf16 rounding midpoint 0x8000.  Within
-// the range the two fp32 values lie fewer than kSiluMargin steps apart, so
-// both round to the same bf16 (an exhaustive check over every fp32 a, on the
-// device, tests exactly this implication).  Outside the range (large |a|,
-// where ex2's argument rounding grows, and where 1 + e overflows) and near
-// a midpoint the caller recomputes canonical_silu.
+// more than m steps from the bf16 rounding midpoint 0x8000, m = 8 for |a| < 4
+// and 24 up to 8.  There the fast and the canonical fp32 values lie at most 6
+// and 16 steps apart (ex2's argument rounding grows with |a|), so both round
+// to the same bf16; an exhaustive check over every fp32 a, on the device,
+// tests exactly this implication.  Outside the range (large |a|, and where
+// 1 + e overflows) and near a midpoint the caller recomputes canonical_silu.
 constexpr float kSiluFastRange = 8.0f;
-constexpr uint32_t kSiluMargin = 32;
 __device__ __forceinline__ bool silu_settled(float a, float v) {
-  const uint32_t d = (__float_as_uint(v) & 0xffffu) - (0x8000u - kSiluMargin);
-  return fabsf(a) <= kSiluFastRange && d > 2u * kSiluMargin;
+  const float fa = fabsf(a);
+  const uint32_t m = fa < 4.0f ? 8u : 24u;
+  const uint32_t d = (__float_as_uint(v) & 0xffffu) - (0x8000u - m);
+  return fa <= kSiluFastRange && d > 2u * m;
 }
 
 }  // namespace afb

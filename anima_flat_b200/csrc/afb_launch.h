@@ -26,10 +26,13 @@ struct DeviceInfo {
 const DeviceInfo& device_info();
 
 // Opt a kernel into `bytes` of dynamic shared memory (cached per kernel).
-cudaError_t ensure_smem_raw(const void* kernel, size_t bytes);
+// max_shared: also prefer the largest shared-memory carveout, for kernels
+// that rely on several CTAs' rings sharing an SM (without it the driver may
+// keep a large L1 and fit one CTA per SM).
+cudaError_t ensure_smem_raw(const void* kernel, size_t bytes, bool max_shared);
 template <typename K>
-cudaError_t ensure_smem(K kernel, size_t bytes) {
-  return ensure_smem_raw(reinterpret_cast<const void*>(kernel), bytes);
+cudaError_t ensure_smem(K kernel, size_t bytes, bool max_shared = false) {
+  return ensure_smem_raw(reinterpret_cast<const void*>(kernel), bytes, max_shared);
 }
 
 // Set by afb_set_pdl(); defaults to on unless AFB_PDL=0 is in the environment.

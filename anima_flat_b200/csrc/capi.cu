@@ -41,7 +41,7 @@ const DeviceInfo& device_info() {
   return cache.emplace(dev, info).first->second;
 }
 
-cudaError_t ensure_smem_raw(const void* kernel, size_t bytes) {
+cudaError_t ensure_smem_raw(const void* kernel, size_t bytes, bool max_shared) {
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, size_t> done;
   int dev = 0;
@@ -52,6 +52,9 @@ cudaError_t ensure_smem_raw(const void* kernel, size_t bytes) {
   if (have >= bytes) return cudaSuccess;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(bytes));
+  if (e == cudaSuccess && max_shared)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess) have = bytes;
   return e;
 }

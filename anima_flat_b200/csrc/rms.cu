@@ -546,7 +546,7 @@ static cudaError_t launch_rms_fwd(RmsArgs a, cudaStream_t st) {
   const int64_t cap = static_cast<int64_t>(dev.sms) * ctas;
   const dim3 grid(static_cast<unsigned>(want < cap ? want : cap));
   auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = ensure_smem(kern, smem);
+    cudaError_t e = ensure_smem(kern, smem, true);
     if (e != cudaSuccess) return e;
     return launch_pdl(kern, grid, dim3(kRmsWarps * 32), smem, st, a);
   };
@@ -570,7 +570,7 @@ static cudaError_t launch_rms_bwd(RmsArgs a, int64_t chunks, cudaStream_t st) {
   const int64_t cap = static_cast<int64_t>(dev.sms) * ctas;
   const dim3 grid(static_cast<unsigned>(want < cap ? want : cap));
   auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = ensure_smem(kern, smem);
+    cudaError_t e = ensure_smem(kern, smem, true);
     if (e != cudaSuccess) return e;
     return launch_pdl(kern, grid, dim3(kRmsWarps * 32), smem, st, a);
   };
