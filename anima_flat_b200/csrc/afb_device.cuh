@@ -669,20 +669,64 @@ __device__ __forceinline__ f2_t fast_silu2(f2_t a) {
   return mul2(a, f2(r0, r1));
 }
 
-// True when bf16(v), v = fast_silu2's value for a, is certainly the bf16
-// rounding of canonical_silu(a): |a| within the fast range and v's low 16 bits
-// more than m steps from the bf16 rounding midpoint 0x8000, m = 8 for |a| < 4
-// and 24 up to 8.  There the fast and the canonical fp32 values lie at most 6
-// and 16 steps apart (ex2's argument rounding grows with |a|), so both round
-// to the same bf16; an exhaustive check over every fp32 a, on the device,
-// tests exactly this implication.  Outside the range (large |a|, and where
-// 1 + e overflows) and near a midpoint the caller recomputes canonical_silu.
+// The bf16 pair of fast_silu2's values v for a, with `settled` set when it
+// is certainly the bf16 rounding of canonical_silu on both elements.  The
+// fast and the canonical fp32 values lie at most 6 fp32 steps apart for
+// |a| < 4 and 16 for |a| <= 8 (ex2's argument rounding grows with |a|), so
+// when v * (1 - eps) and v * (1 + eps), eps = 2^-19 resp. 2^-17 (at least 15
+// resp. 63 steps of v), round to the same bf16, so does the canonical value;
+// that bf16 is the result.  An exhaustive check over every fp32 a, on the
+// device, tests exactly this implication.  Outside |a| <= 8 (and where 1 + e
+// overflows) and near a rounding midpoint the caller recomputes canonical_silu.
 constexpr float kSiluFastRange = 8.0f;
-__device__ __forceinline__ bool silu_settled(float a, float v) {
-  const float fa = fabsf(a);
-  const uint32_t m = fa < 4.0f ? 8u : 24u;
-  const uint32_t d = (__float_as_uint(v) & 0xffffu) - (0x8000u - m);
-  return fa <= kSiluFastRange && d > 2u * m;
+__device__ __forceinline__ uint32_t silu_pair_bf16(f2_t a, f2_t v, bool& settled) {
+  const float fa = fmaxf(fabsf(f2lo(a)), fabsf(f2hi(a)));
+  const bool near = fa < 4.0f;
+  const f2_t lo = mul2(v, splat2(near ? 1.0f - 0x1p-19f : 1.0f - 0x1p-17f));
+  const f2_t hi = mul2(v, splat2(near ? 1.0f + 0x1p-19f : 1.0f + 0x1p-17f));
+  const uint32_t bl = f2bf2(lo), bh = f2bf2(hi);
+  settled = fa <= kSiluFastRange && bl == bh;
+  return bh;
+}
+
+// canonical_sigmoid for a pair of elements with |a| <= 87, without branches,
+// identical to canonical_sigmoid on every such fp32 a (an exhaustive device
+// check tests this).  The steps are canonical_exp's: rint(x * log2e) as the
+// sum with 1.5 * 2^23 (in [2^23, 2^24) the sum rounds to an integer, ties to
+// even, and subtracting the constant back is exact), the same Cody & Waite
+// reduction and polynomial (packed FMAs round like scalar ones), and 2^k from
+// the integer bits of that sum (|k| <= 126, one product).  The correctly
+// rounded reciprocal of d = 1 + e in [1, 2^126) is the special-function
+// unit's estimate y refined by one Newton-Raphson step in Markstein's FMA
+// form: r = 1 - d * y (exact), y + y * r.
+__device__ __forceinline__ f2_t sigmoid_core2(f2_t a) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr f2_t kSign = 0x8000000080000000ull;
+  const f2_t x = a ^ kSign;              // canonical_sigmoid takes exp(-a)
+  const float t0 = __fadd_rn(__fmul_rn(f2lo(x), 1.44269502162933349609375f), kRound);
+  const float t1 = __fadd_rn(__fmul_rn(f2hi(x), 1.44269502162933349609375f), kRound);
+  const f2_t k = sub2(f2(t0, t1), splat2(kRound));
+  f2_t r = fma2(k, splat2(-0.693145751953125f), x);
+  r = fma2(k, splat2(-1.428606765330187e-06f), r);
+  f2_t p = fma2(splat2(1.98412701138295233249664306640625e-04f), r,
+                splat2(1.38888892251998186111450195312500e-03f));
+  p = fma2(p, r, splat2(8.33333376795053482055664062500000e-03f));
+  p = fma2(p, r, splat2(4.16666679084300994873046875000000e-02f));
+  p = fma2(p, r, splat2(1.66666671633720397949218750000000e-01f));
+  p = fma2(p, r, splat2(0.5f));
+  p = fma2(p, r, splat2(1.0f));
+  p = fma2(p, r, splat2(1.0f));
+  // bits of t = 0x4B400000 + k; 2^k = (k + 127) << 23
+  constexpr int kBias = 127 - 0x4B400000;
+  const float e0 = __fmul_rn(f2lo(p), __int_as_float((__float_as_int(t0) + kBias) << 23));
+  const float e1 = __fmul_rn(f2hi(p), __int_as_float((__float_as_int(t1) + kBias) << 23));
+  const float d0 = __fadd_rn(1.0f, e0), d1 = __fadd_rn(1.0f, e1);
+  float y0, y1;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(d0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y1) : "f"(d1));
+  const f2_t d = f2(d0, d1), y = f2(y0, y1);
+  const f2_t rr = fma2(d ^ kSign, y, splat2(1.0f));
+  return fma2(y, rr, y);
 }
 
 }  // namespace afb

@@ -27,7 +27,7 @@
 // the same per-row results); a shuffle unit is a run of source pixels (4
 // output rows each), so every unit is one contiguous range of the input.
 //
-// Forward SiLU: fast_silu2 on the special-function unit; where silu_settled
+// Forward SiLU: fast_silu2 on the special-function unit; where silu_pair_bf16
 // cannot vouch for the bf16 rounding (near a rounding midpoint, or |a| out of
 // the fast range) the element is recomputed with canonical_silu.
 //
@@ -43,7 +43,8 @@
 
 namespace afb {
 
-constexpr int kRmsWarps = 8;  // warps per CTA
+constexpr int kRmsWarps = 8;     // warps per forward CTA
+constexpr int kRmsBwdWarps = 6;  // warps per backward CTA: two CTAs per SM leave ~170 registers a thread
 constexpr int kRmsBaseTilesPerChunk = 8;
 constexpr int64_t kRmsMaxChunks = 32768;        // the finalize kernel's limit
 constexpr int kRmsMaxC = 1024;
@@ -143,11 +144,10 @@ rms_fwd_kernel(const RmsArgs a) {
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * kRmsWarps + warp;
   auto unit_of = [&](int64_t j) { return gw + j * W; };
   auto issued = [&](int64_t j) { return unit_of(j) < units; };
-  auto issue = [&](int64_t j) {
+  auto issue = [&](int64_t j, int s) {  // unit j into stage s = j % nsw
     const int64_t r0 = unit_of(j) * UR;
     const int64_t nr = N - r0 < UR ? N - r0 : UR;
     const uint32_t bytes = static_cast<uint32_t>(nr) * C * 2u;
-    const int s = static_cast<int>(j % nsw);
     const uint32_t bar = smem_addr(&bars[s]);
     uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     mbar_arrive_expect_tx(bar, bytes * NIN);
@@ -157,15 +157,16 @@ rms_fwd_kernel(const RmsArgs a) {
     if (HAS_R) bulk_g2s(smem_addr(st + in_bytes), a.r + r0 * C, bytes, bar);
   };
   if (lane == 0) {
-    for (int j = 0; j < nsw && issued(j); ++j) issue(j);
+    for (int j = 0; j < nsw && issued(j); ++j) issue(j, j);
   }
   float gv[KV][8];
 #pragma unroll
   for (int k = 0; k < KV; ++k) load_g8(a.g + (l + LPR * k) * 8, k < KV - 1 || last_ok, gv[k]);
   const uint32_t w2 = static_cast<uint32_t>(a.W / 2);
+  int s = 0;         // stage of unit j (j % nsw)
+  uint32_t ph = 0;   // its phase parity ((j / nsw) & 1)
   for (int64_t j = 0; issued(j); ++j) {
-    const int s = static_cast<int>(j % nsw);
-    if (!mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
+    if (!mbar_wait(smem_addr(&bars[s]), ph)) {
       if (lane == 0) rms_drain(j, nsw, bars, issued);
       return;
     }
@@ -220,46 +221,49 @@ rms_fwd_kernel(const RmsArgs a) {
       }
       const float rstd = rms_rstd(rms_row_sum<LPR, NVP, KV>(sq), a.sqrt_c);
       const f2_t rr = f2(rstd, rstd);
-      float av[KV][8], o[KV][8];
-      uint32_t redo = 0;  // elements whose fast value is not settled
+      f2_t av[KV][4];
+      uint32_t o[KV][4];  // bf16 pairs of y
+      uint32_t redo = 0;  // pairs whose fast value is not settled
 #pragma unroll
       for (int k = 0; k < KV; ++k) {
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
+        for (int e = 0; e < 4; ++e) {
           // a = (s * rstd) * g: products only, exact in packed form
-          const f2_t x2 = mul2(mul2(f2(sv[k][e], sv[k][e + 1]), rr), f2(gv[k][e], gv[k][e + 1]));
-          const f2_t y2 = fast_silu2(x2);
-          av[k][e] = f2lo(x2);
-          av[k][e + 1] = f2hi(x2);
-          o[k][e] = f2lo(y2);
-          o[k][e + 1] = f2hi(y2);
-          if (!silu_settled(av[k][e], o[k][e])) redo |= 1u << (k * 8 + e);
-          if (!silu_settled(av[k][e + 1], o[k][e + 1])) redo |= 1u << (k * 8 + e + 1);
+          av[k][e] = mul2(mul2(f2(sv[k][2 * e], sv[k][2 * e + 1]), rr), f2(gv[k][2 * e], gv[k][2 * e + 1]));
+          bool ok;
+          o[k][e] = silu_pair_bf16(av[k][e], fast_silu2(av[k][e]), ok);
+          if (!ok) redo |= 1u << (k * 4 + e);
         }
       }
       if (__any_sync(kFull, redo != 0)) {
 #pragma unroll
         for (int k = 0; k < KV; ++k)
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (redo & (1u << (k * 8 + e))) o[k][e] = canonical_silu(av[k][e]);
+          for (int e = 0; e < 4; ++e)
+            if (redo & (1u << (k * 4 + e)))
+              o[k][e] = pack2_rn(canonical_silu(f2lo(av[k][e])), canonical_silu(f2hi(av[k][e])));
       }
       if (rok) {
 #pragma unroll
         for (int k = 0; k < KV; ++k)
-          if (k < KV - 1 || last_ok) st16(a.y + dst + (l + LPR * k) * 8, pack8_rn(o[k]));
+          if (k < KV - 1 || last_ok)
+            st16(a.y + dst + (l + LPR * k) * 8, make_uint4(o[k][0], o[k][1], o[k][2], o[k][3]));
       }
     }
     __syncwarp();
     if (lane == 0 && issued(j + nsw)) {
       fence_proxy_async_smem();
-      issue(j + nsw);
+      issue(j + nsw, s);
+    }
+    if (++s == nsw) {
+      s = 0;
+      ph ^= 1u;
     }
   }
 }
 
 template <int LPR, int NVP, int KV, bool HAS_GS, bool SHUF>
-__global__ void __launch_bounds__(kRmsWarps * 32, 2)
+__global__ void __launch_bounds__(kRmsBwdWarps * 32, 2)
 rms_bwd_kernel(const RmsArgs a) {
   constexpr int T = 32 / LPR;
   constexpr int NIN = HAS_GS ? 3 : 2;
@@ -275,7 +279,7 @@ rms_bwd_kernel(const RmsArgs a) {
   const uint32_t stage_bytes = in_bytes * NIN;
   const int nsw = a.nsw;
   uint8_t* ring = smem + static_cast<size_t>(warp) * nsw * stage_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kRmsWarps) * nsw * stage_bytes) +
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kRmsBwdWarps) * nsw * stage_bytes) +
                    warp * nsw;
   if (lane == 0) {
     for (int s = 0; s < nsw; ++s) mbar_init(smem_addr(&bars[s]), 1);
@@ -287,21 +291,21 @@ rms_bwd_kernel(const RmsArgs a) {
   const int64_t N = a.rows;
   const int64_t chunk_rows = static_cast<int64_t>(a.tpc) * T;
   const int64_t chunks = (N + chunk_rows - 1) / chunk_rows;
-  const int spc = a.tpc / a.ut;  // stages per chunk
-  const int64_t W = static_cast<int64_t>(gridDim.x) * kRmsWarps;
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kRmsWarps + warp;
+  const int spc = a.tpc / a.ut;  // stages per chunk, a power of two
+  const int lg_spc = __ffs(spc) - 1;
+  const int64_t W = static_cast<int64_t>(gridDim.x) * kRmsBwdWarps;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kRmsBwdWarps + warp;
   // Stage j of this warp: chunk gw + (j / spc) * W, rows from (j % spc) * UR.
   // Only the last chunk can reach past the rows, and a warp's chunks come in
   // increasing order, so once a stage starts past the end no later one is
   // copied: the copied stages are a prefix of j and the ring's parity follows j.
-  auto chunk_of = [&](int64_t j) { return gw + (j / spc) * W; };
-  auto row0_of = [&](int64_t j) { return chunk_of(j) * chunk_rows + (j % spc) * UR; };
+  auto chunk_of = [&](int64_t j) { return gw + (j >> lg_spc) * W; };
+  auto row0_of = [&](int64_t j) { return chunk_of(j) * chunk_rows + (j & (spc - 1)) * UR; };
   auto issued = [&](int64_t j) { return chunk_of(j) < chunks && row0_of(j) < N; };
-  auto issue = [&](int64_t j) {
+  auto issue = [&](int64_t j, int s) {  // stage j into ring slot s = j % nsw
     const int64_t r0 = row0_of(j);
     const int64_t nr = N - r0 < UR ? N - r0 : UR;
     const uint32_t bytes = static_cast<uint32_t>(nr) * C * 2u;
-    const int s = static_cast<int>(j % nsw);
     const uint32_t bar = smem_addr(&bars[s]);
     uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     mbar_arrive_expect_tx(bar, bytes * NIN);
@@ -310,7 +314,7 @@ rms_bwd_kernel(const RmsArgs a) {
     if (HAS_GS) bulk_g2s(smem_addr(st + 2 * in_bytes), a.gs + r0 * C, bytes, bar);
   };
   if (lane == 0) {
-    for (int j = 0; j < nsw && issued(j); ++j) issue(j);
+    for (int j = 0; j < nsw && issued(j); ++j) issue(j, j);
   }
   float acc[KV][8];
 #pragma unroll
@@ -319,10 +323,11 @@ rms_bwd_kernel(const RmsArgs a) {
     for (int e = 0; e < 8; ++e) acc[k][e] = 0.0f;
   const uint32_t w2 = static_cast<uint32_t>(a.W / 2);
   const uint32_t Wd = static_cast<uint32_t>(a.W);
+  int s = 0;        // ring slot of stage j (j % nsw)
+  uint32_t ph = 0;  // its phase parity ((j / nsw) & 1)
   for (int64_t j = 0; chunk_of(j) < chunks; ++j) {
     if (issued(j)) {
-      const int s = static_cast<int>(j % nsw);
-      if (!mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
+      if (!mbar_wait(smem_addr(&bars[s]), ph)) {
         if (lane == 0) rms_drain(j, nsw, bars, issued);
         return;
       }
@@ -347,6 +352,7 @@ rms_bwd_kernel(const RmsArgs a) {
           for (int e = 0; e < 8; ++e) f[k][e] = __fmul_rn(f[k][e], f[k][e]);
         }
         const float rstd = rms_rstd(rms_row_sum<LPR, NVP, KV>(f), a.sqrt_c);
+        const f2_t rr = f2(rstd, rstd);
         float dag[KV][8], t[KV][8];
 #pragma unroll
         for (int k = 0; k < KV; ++k) {
@@ -356,16 +362,41 @@ rms_bwd_kernel(const RmsArgs a) {
           unpack8(ok ? lds16(rp + v * 16) : make_uint4(0, 0, 0, 0), sv);
           unpack8(ok ? lds16(rp + in_bytes + v * 16) : make_uint4(0, 0, 0, 0), dv);
           load_g8(a.g + v * 8, ok, gv);
+          // n = s * rstd and a = n * g feed only products: packed.  The
+          // sigmoid of |a| <= 87 takes the branch-free core; the rest (rare)
+          // is redone with canonical_sigmoid.
+          f2_t n2[4], av2[4], sg2[4];
+          uint32_t out = 0;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float n = __fmul_rn(sv[e], rstd);
-            const float av = __fmul_rn(n, gv[e]);
-            const float sg = canonical_sigmoid(av);
-            const float da =
-                __fmul_rn(__fmul_rn(dv[e], sg), __fadd_rn(1.0f, __fmul_rn(av, __fsub_rn(1.0f, sg))));
-            if (rok) acc[k][e] = __fadd_rn(acc[k][e], __fmul_rn(da, n));
-            dag[k][e] = __fmul_rn(da, gv[e]);
-            t[k][e] = __fmul_rn(dag[k][e], n);
+          for (int e = 0; e < 4; ++e) {
+            n2[e] = mul2(f2(sv[2 * e], sv[2 * e + 1]), rr);
+            av2[e] = mul2(n2[e], f2(gv[2 * e], gv[2 * e + 1]));
+            const bool in = fmaxf(fabsf(f2lo(av2[e])), fabsf(f2hi(av2[e]))) <= 87.0f;
+            sg2[e] = sigmoid_core2(in ? av2[e] : f2_t{0});
+            if (!in) out |= 1u << e;
+          }
+          if (__any_sync(kFull, out != 0)) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (out & (1u << e))
+                sg2[e] = f2(canonical_sigmoid(f2lo(av2[e])), canonical_sigmoid(f2hi(av2[e])));
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            // da = (dy * sg) * (1 + a * (1 - sg)); a * (1 - sg) is added: scalar
+            const f2_t u2 = sub2(splat2(1.0f), sg2[e]);
+            const f2_t w2 = f2(__fadd_rn(1.0f, __fmul_rn(f2lo(av2[e]), f2lo(u2))),
+                               __fadd_rn(1.0f, __fmul_rn(f2hi(av2[e]), f2hi(u2))));
+            const f2_t da2 = mul2(mul2(f2(dv[2 * e], dv[2 * e + 1]), sg2[e]), w2);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int i = 2 * e + h;
+              const float da = h ? f2hi(da2) : f2lo(da2);
+              const float n = h ? f2hi(n2[e]) : f2lo(n2[e]);
+              if (rok) acc[k][i] = __fadd_rn(acc[k][i], __fmul_rn(da, n));
+              dag[k][i] = __fmul_rn(da, gv[i]);
+              t[k][i] = __fmul_rn(dag[k][i], n);
+            }
           }
         }
         const float m = __fdiv_rn(rms_row_sum<LPR, NVP, KV>(t), static_cast<float>(C));
@@ -385,11 +416,15 @@ rms_bwd_kernel(const RmsArgs a) {
           unpack8(ok ? lds16(rp + v * 16) : make_uint4(0, 0, 0, 0), sv);
           if (HAS_GS) unpack8(ok ? lds16(rp + 2 * in_bytes + v * 16) : make_uint4(0, 0, 0, 0), gsv);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float n = __fmul_rn(sv[e], rstd);
-            float vds = __fmul_rn(rstd, __fsub_rn(dag[k][e], __fmul_rn(n, m)));
-            if (HAS_GS) vds = __fadd_rn(vds, gsv[e]);
-            o[e] = vds;
+          for (int e = 0; e < 8; e += 2) {
+            const f2_t n2 = mul2(f2(sv[e], sv[e + 1]), rr);  // the same n as above
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float n = h ? f2hi(n2) : f2lo(n2);
+              float vds = __fmul_rn(rstd, __fsub_rn(dag[k][e + h], __fmul_rn(n, m)));
+              if (HAS_GS) vds = __fadd_rn(vds, gsv[e + h]);
+              o[e + h] = vds;
+            }
           }
           if (rok && ok) st16(a.y + src + v * 8, pack8_rn(o));
         }
@@ -397,10 +432,14 @@ rms_bwd_kernel(const RmsArgs a) {
       __syncwarp();
       if (lane == 0 && issued(j + nsw)) {
         fence_proxy_async_smem();
-        issue(j + nsw);
+        issue(j + nsw, s);
       }
     }
-    if ((j + 1) % spc == 0) {  // end of a chunk: stride tree over the row groups
+    if (++s == nsw) {
+      s = 0;
+      ph ^= 1u;
+    }
+    if (((j + 1) & (spc - 1)) == 0) {  // end of a chunk: stride tree over the row groups
       const int64_t chunk = chunk_of(j);
 #pragma unroll
       for (int k = 0; k < KV; ++k)
@@ -427,29 +466,40 @@ rms_bwd_kernel(const RmsArgs a) {
   }
 }
 
-// Every fp32 bit pattern through fast_silu2 / silu_settled against
-// canonical_silu.  stats[0]: settled values whose bf16 differs from the
-// canonical one (must be 0); stats[1]: values with |a| <= 8 that are not
-// settled; stats[2 + sign * 256 + exponent]: the largest distance in fp32
-// steps between the fast and the canonical value (both finite, same sign).
-// Block b covers the patterns [b * 65536, (b + 1) * 65536): one sign, one
-// exponent.
+// Every fp32 bit pattern through the forward's fast SiLU (fast_silu2,
+// silu_pair_bf16 on neighbouring patterns as pairs) and the backward's
+// sigmoid_core2, against canonical_silu and canonical_sigmoid.
+// stats[0]: settled SiLU values whose bf16 differs from the canonical one
+// (must be 0); stats[1]: SiLU values with |a| <= 8 left unsettled;
+// stats[2 + sign * 256 + exponent]: the largest distance in fp32 steps
+// between the fast and the canonical SiLU value (both finite, same sign);
+// stats[514]: inputs with |a| <= 87 where sigmoid_core2 differs from
+// canonical_sigmoid in any bit (must be 0).  Block b covers the patterns
+// [b * 65536, (b + 1) * 65536): one sign, one exponent.
 __global__ void __launch_bounds__(256) silu_probe_kernel(unsigned long long* stats) {
-  __shared__ unsigned int red[3];
-  if (threadIdx.x < 3) red[threadIdx.x] = 0;
+  __shared__ unsigned int red[4];
+  if (threadIdx.x < 4) red[threadIdx.x] = 0;
   __syncthreads();
   const uint32_t base = static_cast<uint32_t>(blockIdx.x) << 16;
-  unsigned int bad = 0, redo = 0, maxd = 0;
+  unsigned int bad = 0, redo = 0, maxd = 0, core_bad = 0;
   for (uint32_t i = threadIdx.x * 2; i < 65536u; i += 2 * blockDim.x) {
     const float a0 = __uint_as_float(base + i), a1 = __uint_as_float(base + i + 1);
-    const f2_t y = fast_silu2(f2(a0, a1));
+    const f2_t av2 = f2(a0, a1);
+    const f2_t y = fast_silu2(av2);
+    bool pair_ok;
+    const uint32_t pb = silu_pair_bf16(av2, y, pair_ok);
+    if (fabsf(a0) <= 87.0f && fabsf(a1) <= 87.0f) {
+      const f2_t sg = sigmoid_core2(av2);
+      core_bad += (__float_as_uint(f2lo(sg)) != __float_as_uint(canonical_sigmoid(a0)));
+      core_bad += (__float_as_uint(f2hi(sg)) != __float_as_uint(canonical_sigmoid(a1)));
+    }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const float av = h ? a1 : a0;
       const float vf = h ? f2hi(y) : f2lo(y);
       const float vc = canonical_silu(av);
-      const bool ok = silu_settled(av, vf);
-      const uint32_t bf = pack2_rn(vf, 0.0f) & 0xffffu, bc = pack2_rn(vc, 0.0f) & 0xffffu;
+      const bool ok = pair_ok;
+      const uint32_t bf = h ? pb >> 16 : pb & 0xffffu, bc = pack2_rn(vc, 0.0f) & 0xffffu;
       if (ok && bf != bc) ++bad;
       if (!ok && fabsf(av) <= 8.0f) ++redo;
       const uint32_t uf = __float_as_uint(vf), uc = __float_as_uint(vc);
@@ -462,11 +512,13 @@ __global__ void __launch_bounds__(256) silu_probe_kernel(unsigned long long* sta
   atomicAdd(&red[0], bad);
   atomicAdd(&red[1], redo);
   atomicMax(&red[2], maxd);
+  atomicAdd(&red[3], core_bad);
   __syncthreads();
   if (threadIdx.x == 0) {
     if (red[0]) atomicAdd(&stats[0], static_cast<unsigned long long>(red[0]));
     if (red[1]) atomicAdd(&stats[1], static_cast<unsigned long long>(red[1]));
     atomicMax(&stats[2 + (base >> 23)], static_cast<unsigned long long>(red[2]));
+    if (red[3]) atomicAdd(&stats[514], static_cast<unsigned long long>(red[3]));
   }
 }
 
@@ -518,8 +570,8 @@ static int64_t rms_chunks(int64_t rows, int C) {
     default: return cudaErrorInvalidValue;                          \
   }
 
-static size_t rms_smem(size_t stage, int nsw) {
-  return kRmsWarps * (stage * nsw + nsw * sizeof(uint64_t));
+static size_t rms_smem(size_t stage, int nsw, int warps = kRmsWarps) {
+  return warps * (stage * nsw + nsw * sizeof(uint64_t));
 }
 
 template <bool HAS_R, bool SHUF>
@@ -562,17 +614,17 @@ static cudaError_t launch_rms_bwd(RmsArgs a, int64_t chunks, cudaStream_t st) {
   const int T = 32 / lpr;
   a.ut = 1;
   const size_t stage = static_cast<size_t>(T) * a.C * 2 * (HAS_GS ? 3 : 2);
-  a.nsw = rms_smem(stage, 3) <= kRmsCtaSmemFor2 ? 3 : 2;  // as deep as two CTAs per SM allow
-  const size_t smem = rms_smem(stage, a.nsw);
+  a.nsw = rms_smem(stage, 3, kRmsBwdWarps) <= kRmsCtaSmemFor2 ? 3 : 2;  // as deep as two CTAs per SM allow
+  const size_t smem = rms_smem(stage, a.nsw, kRmsBwdWarps);
   if (smem > dev.max_smem_optin) return cudaErrorInvalidValue;
   const int ctas = smem <= kRmsCtaSmemFor2 ? 2 : 1;
-  const int64_t want = (chunks + kRmsWarps - 1) / kRmsWarps;
+  const int64_t want = (chunks + kRmsBwdWarps - 1) / kRmsBwdWarps;
   const int64_t cap = static_cast<int64_t>(dev.sms) * ctas;
   const dim3 grid(static_cast<unsigned>(want < cap ? want : cap));
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e = ensure_smem(kern, smem, true);
     if (e != cudaSuccess) return e;
-    return launch_pdl(kern, grid, dim3(kRmsWarps * 32), smem, st, a);
+    return launch_pdl(kern, grid, dim3(kRmsBwdWarps * 32), smem, st, a);
   };
   AFB_RMS_DISPATCH(rms_bwd_kernel, HAS_GS, SHUF, go)
 }
@@ -673,7 +725,7 @@ extern "C" int afb_silu_probe(void* stats, void* stream) {
   ApiGuard g("afb_silu_probe");
   if (!check(stats != nullptr && aligned(stats, 8), "stats is null or misaligned")) return g.fail();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(stats, 0, (2 + 512) * sizeof(unsigned long long), st);
+  cudaError_t e = cudaMemsetAsync(stats, 0, (2 + 512 + 1) * sizeof(unsigned long long), st);
   if (e != cudaSuccess) return g.done(e);
   silu_probe_kernel<<<65536, 256, 0, st>>>(static_cast<unsigned long long*>(stats));
   return g.done(cudaGetLastError());

@@ -140,11 +140,14 @@ int afb_rms_silu(const void* x, const void* residual, const void* gamma, void* s
                  int64_t rows, int64_t H, int64_t W, int64_t channels, int shuffled, void* stream);
 
 /* Test hook: every fp32 input through the forward's fast SiLU and its
- * settle test against the canonical SiLU.  stats: 514 uint64 counters,
- * 8-byte aligned, overwritten: [0] settled inputs whose bf16 result differs
- * from the canonical one (0 when the fast path is sound), [1] unsettled
- * inputs with |a| <= 8, [2 + sign*256 + exponent] the largest fp32-step
- * distance between the fast and canonical values.  No reference counterpart. */
+ * settle test against the canonical SiLU, and through the backward's
+ * branch-free sigmoid against the canonical sigmoid.  stats: 515 uint64
+ * counters, 8-byte aligned, overwritten: [0] settled inputs whose bf16 SiLU
+ * differs from the canonical one (0 when the fast path is sound), [1]
+ * unsettled inputs with |a| <= 8, [2 + sign*256 + exponent] the largest
+ * fp32-step distance between the fast and canonical SiLU values, [514]
+ * inputs with |a| <= 87 whose fast sigmoid differs from the canonical one in
+ * any bit (0 when the backward's sigmoid is exact).  No reference counterpart. */
 int afb_silu_probe(void* stats, void* stream);
 
 /* ----------------------------------------------------------------------- */

@@ -123,12 +123,15 @@ def test_rms_silu_bwd_doubled_chunks(cuda_dev):
 
 def test_silu_fast_path_exhaustive(cuda_dev):
     """Every fp32 input: where the forward keeps the SFU value (settled), its
-    bf16 rounding equals the canonical SiLU's; the recomputed share stays small."""
+    bf16 rounding equals the canonical SiLU's, and the recomputed share stays
+    small; the backward's branch-free sigmoid equals the canonical one bit for
+    bit on every |a| <= 87."""
     from anima_flat_b200 import _lib
 
-    stats = torch.zeros(514, dtype=torch.int64, device=cuda_dev)
+    stats = torch.zeros(515, dtype=torch.int64, device=cuda_dev)
     _lib.call("afb_silu_probe", stats.data_ptr(), torch.cuda.current_stream().cuda_stream)
     st = stats.cpu().numpy().astype(np.uint64)
     assert st[0] == 0, f"{st[0]} settled inputs round differently"
+    assert st[514] == 0, f"{st[514]} inputs where the fast sigmoid differs"
     n_small = 2 * (0x41000000 + 1)  # fp32 values with |a| <= 8
     assert st[1] / n_small < 0.002, f"unsettled share {st[1] / n_small:.4%}"
