@@ -55,7 +55,10 @@ struct FinalizeArgs {
   int seg;
   void* out[3];
   int bf16_out;
-  int np;  // set by the launcher
+  int np;               // set by the launcher
+  int64_t bstride;      // set by the launcher: floats between batch entries of part
+  int64_t nflat;        // set by the launcher: valid floats of a batch entry of part
+  int64_t out_bstride;  // set by the launcher: elements between batch entries of out
 };
 bool finalize_fits(int64_t n);
 cudaError_t launch_colsum_finalize(const FinalizeArgs& f, int64_t batch, cudaStream_t st);
