@@ -321,7 +321,7 @@ static cudaError_t launch_adaln_bwd_stats(const AdalnStatsArgs& a, cudaStream_t 
   const int64_t want = (a.rows + kStatPairs - 1) / kStatPairs;
   const dim3 grid(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
   auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = ensure_smem(kern, smem);
+    cudaError_t e = ensure_smem(kern, smem, true);
     if (e != cudaSuccess) return e;
     return launch_pdl(kern, grid, dim3(kStatWarps * 32), smem, st, a, smods);
   };
@@ -341,6 +341,10 @@ template <bool HAS_X, bool HAS_GZ>
 static cudaError_t launch_adaln_bwd_cols(const AdalnColsArgs& a, int64_t batch, cudaStream_t st) {
   const dim3 grid(static_cast<unsigned>((a.dim + kColCols - 1) / kColCols), static_cast<unsigned>(a.chunks),
                   static_cast<unsigned>(batch));
+  // The same shared-memory carveout as the stats and finalize kernels around
+  // it, so consecutive launches need no reconfiguration of the SMs.
+  cudaError_t e = ensure_smem(adaln_bwd_cols_kernel<HAS_X, HAS_GZ>, 0, true);
+  if (e != cudaSuccess) return e;
   return launch_pdl(adaln_bwd_cols_kernel<HAS_X, HAS_GZ>, grid, dim3(kColWarps * 32), 0, st, a);
 }
 

@@ -43,20 +43,28 @@ const DeviceInfo& device_info() {
 
 cudaError_t ensure_smem_raw(const void* kernel, size_t bytes, bool max_shared) {
   static std::mutex mu;
-  static std::map<std::pair<int, const void*>, size_t> done;
+  struct State {
+    size_t bytes = 0;
+    bool carveout = false;
+  };
+  static std::map<std::pair<int, const void*>, State> done;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lock(mu);
-  size_t& have = done[{dev, kernel}];
-  if (have >= bytes) return cudaSuccess;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(bytes));
-  if (e == cudaSuccess && max_shared)
+  State& have = done[{dev, kernel}];
+  if (have.bytes < bytes) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e != cudaSuccess) return e;
+    have.bytes = bytes;
+  }
+  if (max_shared && !have.carveout) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared);
-  if (e == cudaSuccess) have = bytes;
-  return e;
+    if (e != cudaSuccess) return e;
+    have.carveout = true;
+  }
+  return cudaSuccess;
 }
 
 bool pdl_enabled() {

@@ -35,7 +35,7 @@ template <int COLS>
 __global__ void __launch_bounds__(kFinalizeThreads)
 colsum_finalize_kernel(const FinalizeArgs f) {
   constexpr int RPI = kFinalizeThreads / COLS;  // partial rows per pass of the CTA
-  constexpr int kBatch = 16;                    // loads in flight per thread
+  constexpr int kBatch = 8;                     // loads in flight per thread
   extern __shared__ float sm[];
   pdl_wait();
   pdl_trigger();
@@ -45,14 +45,19 @@ colsum_finalize_kernel(const FinalizeArgs f) {
   const int64_t b = blockIdx.y;
   const int col = blockIdx.x * COLS + c;
   const bool cok = col < f.ncols;
-  const float* part = f.part + b * f.bstride + col;
+  // Rows s = r, r + RPI, ..., kBatch at a time with all their loads issued
+  // before the stores into shared memory; rows past the end (and, in the
+  // strided view, floats past the batch entry's partials) read as zero.
+  const float* p = f.part + b * f.bstride;
+  const int64_t step = static_cast<int64_t>(RPI) * f.ncols;
+  int64_t at = static_cast<int64_t>(r) * f.ncols + col;  // flat index of (row s, this column)
   for (int s0 = r; s0 < f.np; s0 += kBatch * RPI) {
     float v[kBatch];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       const int s = s0 + u * RPI;
-      const int64_t at = static_cast<int64_t>(s) * f.ncols;
-      v[u] = (cok && s < f.n && at + col < f.nflat) ? __ldg(part + at) : 0.0f;
+      v[u] = (cok && s < f.n && at < f.nflat) ? __ldg(p + at) : 0.0f;
+      at += step;
     }
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
@@ -95,7 +100,7 @@ static cudaError_t launch_finalize_one(FinalizeArgs f, int64_t batch, cudaStream
   while (cols > 4 && ((f.ncols + cols - 1) / cols) * batch < 2 * static_cast<int64_t>(dev.sms)) cols >>= 1;
   auto go = [&](auto kern) -> cudaError_t {
     const size_t smem = static_cast<size_t>(np) * cols * sizeof(float);
-    cudaError_t e = ensure_smem(kern, smem);
+    cudaError_t e = ensure_smem(kern, smem, true);
     if (e != cudaSuccess) return e;
     const dim3 grid(static_cast<unsigned>((f.ncols + cols - 1) / cols), static_cast<unsigned>(batch));
     return launch_pdl(kern, grid, dim3(kFinalizeThreads), smem, st, f);

@@ -302,7 +302,7 @@ static cudaError_t launch_headnorm_bwd(const HeadNormBwdArgs& a, int hd, cudaStr
   const int64_t chunks = hn_chunks(a.tokens);
   const dim3 grid(static_cast<unsigned>(chunks < dev.sms ? chunks : dev.sms));
   auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = ensure_smem(kern, smem);
+    cudaError_t e = ensure_smem(kern, smem, true);
     if (e != cudaSuccess) return e;
     return launch_pdl(kern, grid, dim3(kHnbWarps * 32), smem, st, a, nsw);
   };
