@@ -19,8 +19,10 @@ from tests.test_gpu_forward import act, mods, qkv_inputs, rng
 pytestmark = pytest.mark.gpu
 
 
+# (2, 17000, 256): more than 1024 chunks per batch entry, so the parameter
+# gradients take the two-launch finalize, with two batch entries.
 @pytest.mark.parametrize("B,S,D", [(1, 4096, 2048), (2, 37, 2048), (1, 5, 256), (3, 17, 1024),
-                                   (1, 1, 2048), (2, 33, 2040)])
+                                   (1, 1, 2048), (2, 33, 2040), (2, 17000, 256)])
 @pytest.mark.parametrize("has_gz", [True, False])
 def test_residual_adaln_bwd_bit_exact(B, S, D, has_gz, cuda_dev):
     r = rng(B * 100 + S + D + has_gz)
@@ -51,7 +53,8 @@ def test_adaln_bwd_bit_exact(B, S, D, cuda_dev):
     np.testing.assert_array_equal(to_bits(dscale), o["dscale"])
 
 
-@pytest.mark.parametrize("B,S,H,hd", [(1, 4096, 16, 128), (2, 7, 5, 128), (1, 9, 3, 64), (1, 3, 2, 256)])
+@pytest.mark.parametrize("B,S,H,hd", [(1, 4096, 16, 128), (2, 7, 5, 128), (1, 9, 3, 64), (1, 3, 2, 256),
+                                      (1, 9000, 2, 64)])
 def test_qkv_norm_rope_bwd_bit_exact(B, S, H, hd, cuda_dev):
     r = rng(B + S * 3 + H + hd)
     qkv, qw, kw, cos, sin = qkv_inputs(r, B, S, H, hd)
@@ -65,7 +68,7 @@ def test_qkv_norm_rope_bwd_bit_exact(B, S, H, hd, cuda_dev):
     np.testing.assert_array_equal(to_bits(dkw).view(np.uint32), o_dkw.view(np.uint32))
 
 
-@pytest.mark.parametrize("B,S,H,hd", [(1, 4096, 16, 128), (2, 5, 7, 128), (1, 6, 2, 64)])
+@pytest.mark.parametrize("B,S,H,hd", [(1, 4096, 16, 128), (2, 5, 7, 128), (1, 6, 2, 64), (2, 9000, 2, 64)])
 def test_head_norm_bwd_bit_exact(B, S, H, hd, cuda_dev):
     r = rng(B * 5 + S + H + hd)
     x, dy = act(r, (B, S, H * hd)), act(r, (B, S, H, hd), std=1e-2)
