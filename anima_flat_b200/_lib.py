@@ -40,6 +40,7 @@ SIGNATURES: dict[str, tuple] = {
                               ctypes.c_size_t, _P),
     "afb_head_norm_bwd": (_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, ctypes.c_size_t, _P),
     "afb_ctx_scale": (_P, _P, _P, _P, _I, _I, _I, _I, _P),
+    "afb_ctx_scale_rowquant": (_P, _P, _P, _P, _P, _I, _I, _I, _I, _P),
     "afb_ctx_scale_bwd": (_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P),
     "afb_rms_silu": (_P, _P, _P, _P, _P, _I, _I, _I, _I, c_int, _P),
     "afb_rms_silu_bwd": (_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, c_int, _P, ctypes.c_size_t, _P),

@@ -646,6 +646,12 @@ __device__ __forceinline__ f2_t fast_gelu2(f2_t x) {
   return mul2(x, fma2(splat2(0.5f), (y & kAbs) | (x & kSign), splat2(0.5f)));  // copysign(y, x)
 }
 
+// The trimmed cross-attention's gain (src/kernels/ctx_scale.py:8-37):
+// 1 / (1 + exp(ln_pad - lse)), IEEE operations and canonical_exp.
+__device__ __forceinline__ float ctx_gain(float ln_pad, float lse) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, canonical_exp(__fsub_rn(ln_pad, lse))));
+}
+
 // silu(a) = a * sigmoid(a) with sigmoid(a) = RN(1 / RN(1 + canonical_exp(-a))),
 // every step an IEEE fp32 operation (the VAE's rms_silu, src/kernels/rms.py:74).
 // 1/d correctly rounded is the same number whether formed by division or by

@@ -39,10 +39,6 @@ struct CtxScaleArgs {
 
 constexpr int kCtxWarps = 16;
 
-__device__ __forceinline__ float ctx_gain(float ln_pad, float lse) {
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, canonical_exp(__fsub_rn(ln_pad, lse))));
-}
-
 // MAXIT: the most head iterations a token needs (heads * hd <= 2048).
 template <int HD, bool BWD>
 __global__ void __launch_bounds__(kCtxWarps * 32)

@@ -22,6 +22,15 @@
 // amax is the max over those candidates.  The codes can then differ from the
 // canonical ones only where y / s lies within a few fp32 ulps of an e4m3
 // rounding tie.
+//
+// CTX (the trimmed cross-attention's output path, src/model.py:457 with
+// src/attention.py:180): rowquant(ctx_scale(out, lse, ln_pad)) in one pass.
+// A row is one token's H * hd attention outputs; a 16-element chunk lies in
+// one head h, whose gain ctx_gain(ln_pad[b], lse[b, h, s]) scales it, and the
+// product is rounded to bf16 exactly as ctx_scale stores it.  The quantisation
+// of those bf16 values is the exact non-GELU path, so the codes and scales are
+// those of the two ops run one after the other, without writing and reading
+// back the bf16 intermediate.
 #include "afb_device.cuh"
 #include "afb_launch.h"
 
@@ -36,11 +45,17 @@ struct RowquantArgs {
   float* s;           // [rows] fp32
   int64_t rows;
   int K;
+  // CTX only: x is out [B, S, H, hd] (rows = B*S, K = H*hd)
+  const float* lse;     // [B, H, S]
+  const float* ln_pad;  // [B]
+  int64_t seq;
+  int heads;
+  int hd_shift;         // log2(hd)
 };
 
 __host__ __device__ constexpr int rowquant_block_warps(int group) { return group > 4 ? group : 4; }
 
-template <int CPL, int GROUP, bool GELU>
+template <int CPL, int GROUP, bool GELU, bool CTX = false>
 __global__ void __launch_bounds__(rowquant_block_warps(GROUP) * 32)
 rowquant_kernel(const RowquantArgs a) {
   constexpr int BW = rowquant_block_warps(GROUP);
@@ -60,18 +75,29 @@ rowquant_kernel(const RowquantArgs a) {
   float amax = 0.0f;
   {
     uint4 xv[CPL][2];
+    float lse[CPL], lnp = 0.0f;
+    int64_t bb = 0, ss = 0;
+    if (CTX && row_ok) {
+      bb = row / a.seq;
+      ss = row - bb * a.seq;
+      lnp = __ldg(a.ln_pad + bb);
+    }
 #pragma unroll
     for (int c = 0; c < CPL; ++c) {
       const int e = (t + 32 * GROUP * c) * 16;
       const bool ok = row_ok && e < K;
       xv[c][0] = ok ? ld_stream(a.x + base + e) : make_uint4(0, 0, 0, 0);
       xv[c][1] = ok ? ld_stream(a.x + base + e + 8) : make_uint4(0, 0, 0, 0);
+      if (CTX) lse[c] = ok ? __ldg(a.lse + (bb * a.heads + (e >> a.hd_shift)) * a.seq + ss) : 0.0f;
     }
 #pragma unroll
     for (int c = 0; c < CPL; ++c) {
+      // CTX: y = bf16(x * gain), ctx_scale's product and rounding (products only: packed)
+      const f2_t g2 = splat2(CTX ? ctx_gain(lnp, lse[c]) : 1.0f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const f2_t v = bf2f2(word(xv[c][j >> 2], j & 3));
+        f2_t v = bf2f2(word(xv[c][j >> 2], j & 3));
+        if (CTX) v = bf2f2(f2bf2(mul2(v, g2)));
         y2[c][j] = GELU ? fast_gelu2(v) : v;
         amax = fmaxf(amax, fmaxf(fabsf(f2lo(y2[c][j])), fabsf(f2hi(y2[c][j]))));
       }
@@ -166,26 +192,26 @@ static bool rowquant_shape(int64_t K, int* group, int* cpl) {
   return true;
 }
 
-template <int GROUP, bool GELU>
+template <int GROUP, bool GELU, bool CTX>
 static cudaError_t launch_rowquant_g(const RowquantArgs& a, int cpl, cudaStream_t st) {
   constexpr int BW = rowquant_block_warps(GROUP);
   const int rows_per_block = BW / GROUP;
   const dim3 grid(static_cast<unsigned>((a.rows + rows_per_block - 1) / rows_per_block));
   const dim3 block(BW * 32);
-  return cpl == 1 ? launch_pdl(rowquant_kernel<1, GROUP, GELU>, grid, block, 0, st, a)
-                  : launch_pdl(rowquant_kernel<2, GROUP, GELU>, grid, block, 0, st, a);
+  return cpl == 1 ? launch_pdl(rowquant_kernel<1, GROUP, GELU, CTX>, grid, block, 0, st, a)
+                  : launch_pdl(rowquant_kernel<2, GROUP, GELU, CTX>, grid, block, 0, st, a);
 }
 
-template <bool GELU>
+template <bool GELU, bool CTX = false>
 static cudaError_t launch_rowquant(const RowquantArgs& a, cudaStream_t st) {
   int group = 0, cpl = 0;
   if (!rowquant_shape(a.K, &group, &cpl)) return cudaErrorInvalidValue;
   switch (group) {
-    case 1: return launch_rowquant_g<1, GELU>(a, cpl, st);
-    case 2: return launch_rowquant_g<2, GELU>(a, cpl, st);
-    case 4: return launch_rowquant_g<4, GELU>(a, cpl, st);
-    case 8: return launch_rowquant_g<8, GELU>(a, cpl, st);
-    default: return launch_rowquant_g<16, GELU>(a, cpl, st);
+    case 1: return launch_rowquant_g<1, GELU, CTX>(a, cpl, st);
+    case 2: return launch_rowquant_g<2, GELU, CTX>(a, cpl, st);
+    case 4: return launch_rowquant_g<4, GELU, CTX>(a, cpl, st);
+    case 8: return launch_rowquant_g<8, GELU, CTX>(a, cpl, st);
+    default: return launch_rowquant_g<16, GELU, CTX>(a, cpl, st);
   }
 }
 
@@ -217,10 +243,42 @@ extern "C" int afb_rowquant(const void* x, void* q, void* s, int64_t rows, int64
       !check_ptrs({x, q}, {"x", "q"}) || !check_ptr4(s, "s"))
     return g.fail();
   if (rows == 0) return 0;
-  RowquantArgs a{static_cast<const uint16_t*>(x), static_cast<uint8_t*>(q),
-                 static_cast<float*>(s), rows, static_cast<int>(K)};
+  RowquantArgs a{};
+  a.x = static_cast<const uint16_t*>(x);
+  a.q = static_cast<uint8_t*>(q);
+  a.s = static_cast<float*>(s);
+  a.rows = rows;
+  a.K = static_cast<int>(K);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return g.done(gelu ? launch_rowquant<true>(a, st) : launch_rowquant<false>(a, st));
+}
+
+extern "C" int afb_ctx_scale_rowquant(const void* out, const void* lse, const void* ln_pad, void* q,
+                                      void* s, int64_t batch, int64_t seq, int64_t heads,
+                                      int64_t head_dim, void* stream) {
+  ApiGuard g("afb_ctx_scale_rowquant");
+  int group = 0, cpl = 0;
+  if (!check(batch >= 0, "batch must be >= 0") || !check(seq >= 1, "seq must be >= 1") ||
+      !check(head_dim == 64 || head_dim == 128 || head_dim == 256,
+             "head_dim must be 64, 128 or 256, got " + std::to_string(head_dim)) ||
+      !check(heads >= 1 && rowquant_shape(heads * head_dim, &group, &cpl),
+             "heads * head_dim must be in [1, 16384], got " + std::to_string(heads * head_dim)) ||
+      !check_ptrs({out, q}, {"out", "q"}) || !check_ptr4(lse, "lse") || !check_ptr4(ln_pad, "ln_pad") ||
+      !check_ptr4(s, "s"))
+    return g.fail();
+  if (batch == 0) return 0;
+  RowquantArgs a{};
+  a.x = static_cast<const uint16_t*>(out);
+  a.q = static_cast<uint8_t*>(q);
+  a.s = static_cast<float*>(s);
+  a.rows = batch * seq;
+  a.K = static_cast<int>(heads * head_dim);
+  a.lse = static_cast<const float*>(lse);
+  a.ln_pad = static_cast<const float*>(ln_pad);
+  a.seq = seq;
+  a.heads = static_cast<int>(heads);
+  a.hd_shift = head_dim == 64 ? 6 : head_dim == 128 ? 7 : 8;
+  return g.done(launch_rowquant<false, true>(a, static_cast<cudaStream_t>(stream)));
 }
 
 extern "C" int afb_gelu_probe(const void* x, void* fast, void* canon, int64_t n, void* stream) {

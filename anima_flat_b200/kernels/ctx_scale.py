@@ -15,7 +15,7 @@ import torch
 from .._lib import call
 from .common import _check, _stream
 
-__all__ = ["ctx_scale"]
+__all__ = ["ctx_scale", "ctx_scale_rowquant"]
 
 
 @torch.library.custom_op("anima_flat_b200::ctx_scale", mutates_args=())
@@ -83,3 +83,48 @@ def ctx_scale(out: torch.Tensor, lse: torch.Tensor, ln_pad: torch.Tensor) -> tor
     if out.dtype != torch.bfloat16:
         raise ValueError(f"out must be torch.bfloat16, got {out.dtype}")
     return _ctx_scale(out.contiguous(), lse.float().contiguous(), ln_pad.float().contiguous())
+
+
+@torch.library.custom_op("anima_flat_b200::ctx_scale_rowquant", mutates_args=())
+def _ctx_scale_rowquant(
+    out: torch.Tensor, lse: torch.Tensor, ln_pad: torch.Tensor
+) -> tuple[torch.Tensor, torch.Tensor]:
+    B, S, H, hd = out.shape
+    q = torch.empty(B, S, H * hd, dtype=torch.float8_e4m3fn, device=out.device)
+    s = torch.empty(B * S, 1, dtype=torch.float32, device=out.device)
+    call("afb_ctx_scale_rowquant", out.data_ptr(), lse.data_ptr(), ln_pad.data_ptr(), q.data_ptr(),
+         s.data_ptr(), B, S, H, hd, _stream(out))
+    return q, s
+
+
+@_ctx_scale_rowquant.register_fake
+def _(out, lse, ln_pad):
+    B, S, H, hd = out.shape
+    return (out.new_empty((B, S, H * hd), dtype=torch.float8_e4m3fn),
+            out.new_empty((B * S, 1), dtype=torch.float32))
+
+
+def ctx_scale_rowquant(
+    out: torch.Tensor, lse: torch.Tensor, ln_pad: torch.Tensor
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``rowquant(ctx_scale(out, lse, ln_pad).flatten(2))`` in one pass.
+
+    The FP8 forward quantises the trimmed cross-attention's output right after
+    its gain (src/model.py:457 with src/attention.py:180).  This returns the
+    same codes and scales, bit for bit, without writing the bf16 scaled output.
+    Inference only (FP8 has no backward), like rowquant.
+
+    Args:
+        out: Attention output over the kept keys, [B, S, H, hd] bf16.
+        lse: Its log-sum-exp, [B, H, S] (cast to fp32).
+        ln_pad: log of the number of removed padding keys, [B] (cast to fp32).
+
+    Returns:
+        ``(q, s)``: q [B, S, H*hd] float8_e4m3fn, s [B*S, 1] fp32.
+    """
+    _check(out, lse, ln_pad)
+    if out.ndim != 4 or lse.shape != (out.shape[0], out.shape[2], out.shape[1]):
+        raise ValueError("out must be [B, S, H, hd] and lse [B, H, S]")
+    if out.dtype != torch.bfloat16:
+        raise ValueError(f"out must be torch.bfloat16, got {out.dtype}")
+    return _ctx_scale_rowquant(out.contiguous(), lse.float().contiguous(), ln_pad.float().contiguous())

@@ -90,6 +90,11 @@ def bytes_ctx_scale(s: Shape) -> int:
     return s.rows * s.heads * s.head_dim * 2 * 2 + s.rows * s.heads * 4 + s.batch * 4
 
 
+def bytes_ctx_scale_rowquant(s: Shape) -> int:
+    # out read; q (1 B per element) and s [rows] fp32 written; lse, ln_pad read
+    return s.rows * s.heads * s.head_dim * (2 + 1) + s.rows * 4 + s.rows * s.heads * 4 + s.batch * 4
+
+
 def bytes_ctx_scale_bwd(s: Shape) -> int:
     # out, dy read, dout written; lse read, dlse written; ln_pad
     return s.rows * s.heads * s.head_dim * 2 * 3 + s.rows * s.heads * 4 * 2 + s.batch * 4
@@ -151,6 +156,7 @@ def call_bytes(name: str, s: Shape) -> int:
         "head_norm_bwd": bytes_head_norm_bwd,
         "ctx_scale": bytes_ctx_scale,
         "ctx_scale_bwd": bytes_ctx_scale_bwd,
+        "ctx_scale_rowquant": bytes_ctx_scale_rowquant,
         "rms_silu": lambda sh: bytes_rms("rms_silu"),
         "add_rms_silu": lambda sh: bytes_rms("add_rms_silu"),
         "shuffle_rms_silu": lambda sh: bytes_rms("shuffle_rms_silu"),

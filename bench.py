@@ -663,8 +663,8 @@ def run_reference(args, world, rank):
 # ------------------------------------------------------------- per-op table --
 PER_OPS = ["residual_adaln", "adaln", "qkv_norm_rope", "head_norm", "residual_adaln_fp8",
            "adaln_fp8", "rowquant", "rowquant_gelu", "residual_adaln_bwd", "adaln_bwd",
-           "qkv_norm_rope_bwd", "head_norm_bwd", "ctx_scale", "ctx_scale_bwd", "rms_silu",
-           "add_rms_silu", "shuffle_rms_silu", "rms_silu_bwd"]
+           "qkv_norm_rope_bwd", "head_norm_bwd", "ctx_scale", "ctx_scale_bwd", "ctx_scale_rowquant",
+           "rms_silu", "add_rms_silu", "shuffle_rms_silu", "rms_silu_bwd"]
 
 
 def run_per_op(args):
@@ -682,7 +682,7 @@ def run_per_op(args):
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
     names = PER_OPS if args.op == "all" else args.op.split(",")
     for name in names:
-        fp8 = name in ("residual_adaln_fp8", "adaln_fp8", "rowquant", "rowquant_gelu")
+        fp8 = name in ("residual_adaln_fp8", "adaln_fp8", "rowquant", "rowquant_gelu", "ctx_scale_rowquant")
         s = W.Shape(batch=args.op_batch or (2 if fp8 else 1))
         B, S, D, H, hd = s.batch, s.seq, s.dim, s.heads, s.head_dim
         g = torch.Generator(device=device).manual_seed(7)
@@ -740,10 +740,14 @@ def run_per_op(args):
                 sets = [(act(1, side, side, Cv), gam, act(1, side, side, Cv) * 0.01,
                          act(1, side, side, Cv) * 0.01, False) for _ in range(nbuf)]
                 fn = ops.rms_silu_bwd
-        elif name in ("ctx_scale", "ctx_scale_bwd"):  # cross-attention output at config 2
+        elif name in ("ctx_scale", "ctx_scale_bwd", "ctx_scale_rowquant"):
+            # cross-attention output: config 2 for the bf16 ops, config 3 (B=2) for the FP8 one
             lse = lambda: 2.0 + 4.0 * torch.randn(B, H, S, generator=g, device=device)
             lnp = torch.full((B,), 4.0, device=device)
-            if name == "ctx_scale":
+            if name == "ctx_scale_rowquant":
+                sets = [(act(B, S, H, hd), lse(), lnp) for _ in range(nbuf)]
+                fn = afb.ctx_scale_rowquant
+            elif name == "ctx_scale":
                 sets = [(act(B, S, H, hd), lse(), lnp) for _ in range(nbuf)]
                 fn = afb.ctx_scale
             else:

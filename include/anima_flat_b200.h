@@ -223,6 +223,19 @@ int afb_ctx_scale_bwd(const void* out, const void* lse, const void* ln_pad, cons
                       void* dout, void* dlse, int64_t batch, int64_t seq, int64_t heads,
                       int64_t head_dim, void* stream);
 
+/* The trimmed cross-attention's output path of the FP8 forward in one pass:
+ * replaces rowquant(ctx_scale(out, lse, ln_pad).flatten(2)), i.e.
+ * src/model.py:457 after src/attention.py:180 (ctx_scale.py:8-37, then
+ * fp8.py:273-301).  A fusion the reference does not have: q and s equal
+ * those of the two entry points run one after the other, bit for bit, and
+ * the bf16 intermediate is never written.  out [batch, seq, heads, head_dim]
+ * bf16; lse [batch, heads, seq], ln_pad [batch] fp32 -> q [batch, seq,
+ * heads*head_dim] e4m3, s [batch*seq] fp32.  head_dim 64, 128 or 256;
+ * heads*head_dim <= 16384. */
+int afb_ctx_scale_rowquant(const void* out, const void* lse, const void* ln_pad, void* q, void* s,
+                           int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
+                           void* stream);
+
 /* Replaces src/kernels/rms.py:200-243 (anima_flat::rms_silu_bwd, launching
  * _bwd_kernel, rms.py:76-125; partials reduced here in a fixed order instead
  * of torch .sum).  s [rows, C] (the saved s or x); dy [rows, C]; gs (the

@@ -218,6 +218,14 @@ def ctx_scale(out, lse, ln_pad, dy=None, mode=RNE):
     return dout, dlse
 
 
+def ctx_scale_rowquant(out, lse, ln_pad, mode=RNE):
+    """rowquant(ctx_scale(out, lse, ln_pad).flatten(2)): the two restatements
+    one after the other.  Returns (q [B, S, H*hd] uint8, s [B*S, 1] f32)."""
+    y = ctx_scale(out, lse, ln_pad, mode=mode)
+    B, S, H, hd = y.shape
+    return rowquant(y.reshape(B, S, H * hd), mode=mode)
+
+
 def rms_lpr(C: int) -> int:
     """Lanes per row of the canonical rms order (P of its row sums)."""
     return int(lib().orc_rms_lpr(C))

@@ -92,6 +92,16 @@ def test_ctx_scale_rejects_bad_shapes():
     assert _status("afb_ctx_scale", FAKE, FAKE, FAKE, FAKE, 0, 4, 16, 128, None)[0] == 0
 
 
+def test_ctx_scale_rowquant_rejects_bad_shapes():
+    rc, msg = _status("afb_ctx_scale_rowquant", FAKE, FAKE, FAKE, FAKE, FAKE, 1, 4, 16, 96, None)
+    assert rc == 1 and "afb_ctx_scale_rowquant" in msg and "head_dim" in msg
+    rc, msg = _status("afb_ctx_scale_rowquant", FAKE, FAKE, FAKE, FAKE, FAKE, 1, 4, 256, 128, None)
+    assert rc == 1 and "heads * head_dim" in msg
+    rc, msg = _status("afb_ctx_scale_rowquant", FAKE, FAKE, FAKE, FAKE, FAKE + 2, 1, 4, 16, 128, None)
+    assert rc == 1 and "s is not 4-byte aligned" in msg
+    assert _status("afb_ctx_scale_rowquant", FAKE, FAKE, FAKE, FAKE, FAKE, 0, 4, 16, 128, None)[0] == 0
+
+
 def test_rms_silu_rejects_bad_channels_and_grid():
     rc, msg = _status("afb_rms_silu", FAKE, None, FAKE, None, FAKE, 4, 0, 0, 100, 0, None)
     assert rc == 1 and "afb_rms_silu" in msg and "multiple of 8" in msg

@@ -82,3 +82,36 @@ def test_ctx_scale_rejects_bad_shapes(cuda_dev):
         afb.ctx_scale(out, torch.zeros(1, 4, 2, device=cuda_dev), torch.zeros(1, device=cuda_dev))
     with pytest.raises(ValueError):
         afb.ctx_scale(out.cpu(), torch.zeros(1, 2, 4), torch.zeros(1))
+
+
+# The trimmed cross-attention output path of the FP8 forward in one pass.
+FUSED_CASES = [(2, 4096, 16, 128), (1, 37, 5, 64), (3, 9, 8, 256), (2, 300, 3, 128), (1, 5, 64, 256)]
+
+
+@pytest.mark.parametrize("B,S,H,hd", FUSED_CASES)
+def test_ctx_scale_rowquant_equals_the_two_ops(B, S, H, hd, cuda_dev):
+    """Codes and scales equal rowquant(ctx_scale(...)) on the device and the
+    oracle's composition of the two, bit for bit; saturated gains included.
+    (The fused op takes rows up to 16384 wide; ctx_scale alone up to 2048, so
+    wider cases compare with the oracle only.)"""
+    out, lse, ln_pad, _ = _inputs(B, S, H, hd, B * 300 + S + H + hd)
+    lse[:, :, ::7] = -150.0
+    lse[:, :, 3::7] = 300.0
+    o, l_, lp = from_bits(out, cuda_dev), torch.from_numpy(lse).to(cuda_dev), torch.from_numpy(ln_pad).to(cuda_dev)
+    q, s = afb.ctx_scale_rowquant(o, l_, lp)
+    assert q.shape == (B, S, H * hd) and q.dtype == torch.float8_e4m3fn and s.shape == (B * S, 1)
+    if H * hd <= 2048:
+        rq, rs = afb.rowquant(afb.ctx_scale(o, l_, lp).flatten(2))
+        assert torch.equal(q.view(torch.uint8), rq.view(torch.uint8))
+        assert torch.equal(s.view(torch.int32), rs.view(torch.int32))
+    oq, os_ = C.ctx_scale_rowquant(out, lse, ln_pad)
+    np.testing.assert_array_equal(q.view(torch.uint8).cpu().numpy(), oq)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), os_.view(np.uint32))
+
+
+def test_ctx_scale_rowquant_rejects_bad_shapes(cuda_dev):
+    out = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16, device=cuda_dev)
+    with pytest.raises(ValueError):
+        afb.ctx_scale_rowquant(out, torch.zeros(1, 4, 2, device=cuda_dev), torch.zeros(1, device=cuda_dev))
+    with pytest.raises(ValueError):
+        afb.ctx_scale_rowquant(out.float(), torch.zeros(1, 2, 4, device=cuda_dev), torch.zeros(1, device=cuda_dev))
