@@ -128,38 +128,6 @@ __device__ __forceinline__ uint2 e4m3x8(const float (&f)[8]) {
   return r;
 }
 
-// Whether the e4m3 code of q = RN(y * RN(1/s)) is certainly the code of the
-// correctly rounded quotient Q = RN(y / s).  RN(1/s) has relative error at
-// most 2^-24, so |y * RN(1/s) - y/s| < 1 ulp and |q - Q| <= 1 ulp.  For
-// |q| >= 2^-6 (the e4m3 normal range) e4m3 keeps 3 of the 23 fp32 mantissa
-// bits, and its rounding midpoints are the values whose low 20 mantissa bits
-// are 0x80000; q and Q round alike unless q lies within 1 ulp of one.  The
-// test rejects a 2-ulp window around each midpoint, everything below 2^-6
-// (the e4m3 subnormal grid), and NaN.
-__device__ __forceinline__ bool e4m3_code_settled(float q) {
-  const uint32_t u = __float_as_uint(q);
-  return ((u - 0x7fffeu) & 0xfffffu) > 4u && fabsf(q) >= 0x1p-6f;
-}
-
-// e4m3 codes of clamp(RN(y[k] / s), +-448): the product by r = RN(1/s) when
-// every code of the vector is settled, else the IEEE quotient.
-__device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, float r) {
-  float q[8];
-  bool settled = true;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    q[k] = __fmul_rn(y[k], r);
-    settled = settled && e4m3_code_settled(q[k]);
-  }
-  if (!settled) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) q[k] = __fdiv_rn(y[k], s);
-  }
-#pragma unroll
-  for (int k = 0; k < 8; ++k) q[k] = clamp448(q[k]);
-  return e4m3x8(q);
-}
-
 // ---------------------------------------------------------------------------
 // Canonical sums.
 // ---------------------------------------------------------------------------
@@ -347,6 +315,37 @@ __device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
 __device__ __forceinline__ f2_t bf2f2(uint32_t w) { return f2(bf_lo(w), bf_hi(w)); }
 // fp32 pair -> bf16 pair, round to nearest even.
 __device__ __forceinline__ uint32_t f2bf2(f2_t v) { return pack2_rn(f2lo(v), f2hi(v)); }
+
+// e4m3 codes of clamp(RN(y[k] / s), +-448).  r = RN(1/s) has relative error
+// at most 2^-24, so q = RN(y * r) lies within 1 ulp of the correctly rounded
+// quotient Q = RN(y / s).  Each pair converts q * (1 - 2^-22) and q * (1 + 2^-22),
+// at least 1.5 ulp below and above q after rounding, so Q lies between them;
+// e4m3 rounding (saturating) is monotone, so when both ends give the same
+// code, that is Q's code, and it is the result.  The lower end alone is
+// clamped, so a NaN quotient (clamped to -448 by the reference) never
+// matches and takes the exact path.  Where any pair of the vector is open,
+// all eight codes come from the IEEE quotient.
+__device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, float r) {
+  const f2_t rr = f2(r, r);
+  uint32_t hi[4];
+  bool settled = true;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const f2_t q = mul2(f2(y[2 * j], y[2 * j + 1]), rr);
+    const f2_t a = mul2(q, f2(1.0f - 0x1p-22f, 1.0f - 0x1p-22f));
+    const f2_t b = mul2(q, f2(1.0f + 0x1p-22f, 1.0f + 0x1p-22f));
+    hi[j] = e4m3x2(f2lo(b), f2hi(b));
+    settled = settled && e4m3x2(clamp448(f2lo(a)), clamp448(f2hi(a))) == hi[j];
+  }
+  if (!settled) {
+    float q[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) q[k] = clamp448(__fdiv_rn(y[k], s));
+    return e4m3x8(q);
+  }
+  return make_uint2(hi[0] | (hi[1] << 16), hi[2] | (hi[3] << 16));
+}
+
 // Element-wise scalar products of two pairs, kept scalar so that they are never
 // contracted into a following add.
 __device__ __forceinline__ f2_t mul2_noc(f2_t a, f2_t b) {
