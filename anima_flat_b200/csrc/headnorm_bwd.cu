@@ -12,9 +12,11 @@
 // v's gradient is copied into the v third of dqkv (rope.py:304-326).
 //
 // Layout: persistent CTAs of kHnbWarps warps walk fixed chunks of kHnbWarps
-// tokens; warp w takes token w of each chunk.  Lane 0 streams the token's
-// forward input (the contiguous q|k span, or x) and upstream gradients into a
-// shared-memory stage with bulk copies completing on an mbarrier.  A head
+// tokens; warp w takes token w of each chunk.  The unit of the warp's ring of
+// shared-memory stages is one section of one token (q or k, or x): lane 0
+// streams the section's forward input and its upstream gradient into a stage
+// with bulk copies completing on an mbarrier, up to nsw units ahead, so the
+// next section's bytes are in flight while the warp computes.  A head
 // spans L = hd/16 lanes; lane l holds dims [8l, 8l+8) of both halves, so the
 // rotation pairs are in the lane and the per-head sums follow the forward's
 // canonical order.
@@ -30,7 +32,7 @@
 namespace afb {
 
 constexpr int kHnbWarps = 8;       // warps per CTA = tokens per chunk
-constexpr int kHnbMaxStages = 4;
+constexpr int kHnbMaxStages = 3;
 constexpr int kHnbUnroll = 2;
 
 struct HeadNormBwdArgs {
@@ -67,8 +69,8 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
   const int H = a.heads;
   const int iters = (H + HPI - 1) / HPI;
   const uint32_t sec_bytes = static_cast<uint32_t>(H) * HD * 2u;
-  // stage: forward input sections (contiguous), then one upstream gradient per section
-  const uint32_t stage_bytes = 2u * NSEC * sec_bytes;
+  // stage: one section's forward input, then its upstream gradient
+  const uint32_t stage_bytes = 2u * sec_bytes;
   float* xch = reinterpret_cast<float*>(smem);  // [warps][NSEC][HD] token sums
   uint8_t* ring = smem + kHnbWarps * NSEC * HD * sizeof(float) +
                   static_cast<size_t>(warp) * nsw * stage_bytes;
@@ -89,20 +91,29 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
     return (static_cast<int64_t>(blockIdx.x) + j * gridDim.x) * kHnbWarps + warp;
   };
   auto chunk_of = [&](int64_t j) { return static_cast<int64_t>(blockIdx.x) + j * gridDim.x; };
-  auto issue = [&](int64_t j) {  // lane 0
-    const int64_t tok = token_of(j);
-    const int s = static_cast<int>(j % nsw);
+  // Unit u of this warp: section u % NSEC of its token u / NSEC.  Units of
+  // tokens past the end are neither copied nor waited for; a warp's tokens
+  // increase with u, so the copied units are a prefix and the ring's slot
+  // (u % nsw) and phase ((u / nsw) & 1) follow u.
+  auto unit_exists = [&](int64_t u) {
+    const int64_t j = u / NSEC;
+    return chunk_of(j) < chunks && token_of(j) < a.tokens;
+  };
+  auto issue = [&](int64_t u, int s) {  // lane 0: unit u into slot s
+    const int64_t tok = token_of(u / NSEC);
+    const int sec = static_cast<int>(u % NSEC);
     uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
     mbar_arrive_expect_tx(bar, stage_bytes);
-    bulk_g2s(smem_addr(st), a.src + tok * a.src_row + a.q_off, NSEC * sec_bytes, bar);
-    bulk_g2s(smem_addr(st + NSEC * sec_bytes), a.dq + tok * static_cast<int64_t>(H) * HD, sec_bytes, bar);
-    if (WITH_K)
-      bulk_g2s(smem_addr(st + 3 * sec_bytes), a.dk + tok * static_cast<int64_t>(H) * HD, sec_bytes, bar);
+    bulk_g2s(smem_addr(st), a.src + tok * a.src_row + (sec ? a.k_off : a.q_off), sec_bytes, bar);
+    bulk_g2s(smem_addr(st + sec_bytes), (sec ? a.dk : a.dq) + tok * static_cast<int64_t>(H) * HD, sec_bytes,
+             bar);
   };
   if (lane == 0) {
-    for (int j = 0; j < nsw && chunk_of(j) < chunks && token_of(j) < a.tokens; ++j) issue(j);
+    for (int u = 0; u < nsw && unit_exists(u); ++u) issue(u, u);
   }
+  int slot = 0;      // ring slot of the next unit
+  uint32_t ph = 0;   // its phase parity
 
   float w[NSEC][2][8];
 #pragma unroll
@@ -117,6 +128,7 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
   }
 
   bool dead = false;  // set if a bounded wait gave up: the warp then only joins the barriers
+  int64_t u = 0;      // this warp's next unit
   for (int64_t j = 0; chunk_of(j) < chunks; ++j) {
     const int64_t tok = token_of(j);
     const bool has = tok < a.tokens && !dead;
@@ -128,8 +140,6 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) wacc[sec][hf][k] = 0.0f;
     if (has) {
-      const int s = static_cast<int>(j % nsw);
-      const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
       float cs[8], sn[8];
       if (ROTATE) {
         const int64_t pos = tok % a.seq;
@@ -147,15 +157,18 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
         uint16_t* out = a.dsrc + tok * a.src_row + a.v_off;
         for (int v = lane; v < H * HD / 8; v += 32) st16(out + 8 * v, ld_stream(in + 8 * v));
       }
-      if (!mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
-        for (int64_t k = j + 1; k < j + nsw && chunk_of(k) < chunks && token_of(k) < a.tokens; ++k)
-          mbar_wait(smem_addr(&bars[k % nsw]), static_cast<uint32_t>((k / nsw) & 1));
-        dead = true;
-      }
 #pragma unroll
-      for (int sec = 0; sec < NSEC && !dead; ++sec) {
-        const uint8_t* xin = st + sec * sec_bytes;
-        const uint8_t* gin = st + (NSEC + sec) * sec_bytes;
+      for (int sec = 0; sec < NSEC; ++sec) {
+        const uint8_t* st = ring + static_cast<size_t>(slot) * stage_bytes;
+        if (!mbar_wait(smem_addr(&bars[slot]), ph)) {
+          // Never expected: wait (bounded) for the copies still in flight, then stop.
+          for (int64_t k = u + 1; k < u + nsw && unit_exists(k); ++k)
+            mbar_wait(smem_addr(&bars[k % nsw]), static_cast<uint32_t>((k / nsw) & 1));
+          dead = true;
+          break;
+        }
+        const uint8_t* xin = st;
+        const uint8_t* gin = st + sec_bytes;
         uint16_t* out = a.dsrc + tok * a.src_row + (sec ? a.k_off : a.q_off);
         for (int it0 = 0; it0 < iters; it0 += kHnbUnroll) {
           uint4 xa[kHnbUnroll], xb[kHnbUnroll];
@@ -239,11 +252,16 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
             st16(out + h * HD + HALF + 8 * l, pack8_rn(ob));
           }
         }
-      }
-      __syncwarp();
-      if (lane == 0 && !dead && chunk_of(j + nsw) < chunks && token_of(j + nsw) < a.tokens) {
-        fence_proxy_async_smem();
-        issue(j + nsw);
+        __syncwarp();  // the stage is read: refill it with unit u + nsw
+        if (lane == 0 && unit_exists(u + nsw)) {
+          fence_proxy_async_smem();
+          issue(u + nsw, slot);
+        }
+        ++u;
+        if (++slot == nsw) {
+          slot = 0;
+          ph ^= 1u;
+        }
       }
     }
     // token sum: stride tree over the lane groups (xor 16, then 8, ... down to L)
@@ -292,7 +310,7 @@ static cudaError_t launch_headnorm_bwd(const HeadNormBwdArgs& a, int hd, cudaStr
   const DeviceInfo& dev = device_info();
   if (dev.error != cudaSuccess) return dev.error;
   constexpr int NSEC = WITH_K ? 2 : 1;
-  const size_t stage = 2 * NSEC * static_cast<size_t>(a.heads) * hd * 2;
+  const size_t stage = 2 * static_cast<size_t>(a.heads) * hd * 2;  // one section: input + gradient
   const size_t fixed = static_cast<size_t>(kHnbWarps) * NSEC * hd * sizeof(float);
   const size_t per = kHnbWarps * (stage + sizeof(uint64_t));
   int nsw = static_cast<int>((dev.max_smem_optin - fixed) / per);
