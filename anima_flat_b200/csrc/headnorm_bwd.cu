@@ -33,7 +33,8 @@ namespace afb {
 
 constexpr int kHnbWarps = 8;       // warps per CTA = tokens per chunk
 constexpr int kHnbMaxStages = 3;
-constexpr int kHnbUnroll = 2;
+constexpr size_t kHnbCtaSmemFor2 = 110 * 1024;  // two CTAs per SM at or below this
+constexpr int kHnbUnroll = 1;
 
 struct HeadNormBwdArgs {
   const uint16_t* src;  // forward input rows (qkv or x)
@@ -55,7 +56,7 @@ struct HeadNormBwdArgs {
 };
 
 template <int HD, bool ROTATE, bool WITH_K, bool WITH_V>
-__global__ void __launch_bounds__(kHnbWarps * 32, 1)
+__global__ void __launch_bounds__(kHnbWarps * 32, 2)
 headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
   constexpr int L = HD / 16;
   constexpr int HPI = 32 / L;
@@ -115,30 +116,11 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
   int slot = 0;      // ring slot of the next unit
   uint32_t ph = 0;   // its phase parity
 
-  float w[NSEC][2][8];
-#pragma unroll
-  for (int sec = 0; sec < NSEC; ++sec) {
-    const float* wp = (sec ? a.wk : a.wq) + 8 * l;
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const float4 w0 = ld_keep_f4(wp + hf * HALF), w1 = ld_keep_f4(wp + hf * HALF + 4);
-      w[sec][hf][0] = w0.x; w[sec][hf][1] = w0.y; w[sec][hf][2] = w0.z; w[sec][hf][3] = w0.w;
-      w[sec][hf][4] = w1.x; w[sec][hf][5] = w1.y; w[sec][hf][6] = w1.z; w[sec][hf][7] = w1.w;
-    }
-  }
-
   bool dead = false;  // set if a bounded wait gave up: the warp then only joins the barriers
   int64_t u = 0;      // this warp's next unit
   for (int64_t j = 0; chunk_of(j) < chunks; ++j) {
     const int64_t tok = token_of(j);
     const bool has = tok < a.tokens && !dead;
-    float wacc[NSEC][2][8];
-#pragma unroll
-    for (int sec = 0; sec < NSEC; ++sec)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) wacc[sec][hf][k] = 0.0f;
     if (has) {
       float cs[8], sn[8];
       if (ROTATE) {
@@ -169,6 +151,19 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
         }
         const uint8_t* xin = st;
         const uint8_t* gin = st + sec_bytes;
+        // The section's norm weights (L1-resident) and its weight-gradient sums.
+        float w[2][8], wacc[2][8];
+        {
+          const float* wp = (sec ? a.wk : a.wq) + 8 * l;
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const float4 w0 = ld_keep_f4(wp + hf * HALF), w1 = ld_keep_f4(wp + hf * HALF + 4);
+            w[hf][0] = w0.x; w[hf][1] = w0.y; w[hf][2] = w0.z; w[hf][3] = w0.w;
+            w[hf][4] = w1.x; w[hf][5] = w1.y; w[hf][6] = w1.z; w[hf][7] = w1.w;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) wacc[hf][k] = 0.0f;
+          }
+        }
         uint16_t* out = a.dsrc + tok * a.src_row + (sec ? a.k_off : a.q_off);
         for (int it0 = 0; it0 < iters; it0 += kHnbUnroll) {
           uint4 xa[kHnbUnroll], xb[kHnbUnroll];
@@ -219,8 +214,8 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
             unpack8(xb[u], fb);
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-              ta[k] = __fmul_rn(__fmul_rn(dpa[u][k], w[sec][0][k]), __fmul_rn(fa[k], rstd[u]));
-              tb[k] = __fmul_rn(__fmul_rn(dpb[u][k], w[sec][1][k]), __fmul_rn(fb[k], rstd[u]));
+              ta[k] = __fmul_rn(__fmul_rn(dpa[u][k], w[0][k]), __fmul_rn(fa[k], rstd[u]));
+              tb[k] = __fmul_rn(__fmul_rn(dpb[u][k], w[1][k]), __fmul_rn(fb[k], rstd[u]));
             }
             cc[u] = __fadd_rn(vec_sum8(ta), vec_sum8(tb));
           }
@@ -241,16 +236,31 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
             for (int k = 0; k < 8; ++k) {
               const float xha = __fmul_rn(fa[k], rstd[u]);
               const float xhb = __fmul_rn(fb[k], rstd[u]);
-              const float ua = __fmul_rn(dpa[u][k], w[sec][0][k]);
-              const float ub = __fmul_rn(dpb[u][k], w[sec][1][k]);
+              const float ua = __fmul_rn(dpa[u][k], w[0][k]);
+              const float ub = __fmul_rn(dpb[u][k], w[1][k]);
               oa[k] = __fmul_rn(rstd[u], __fsub_rn(ua, __fmul_rn(xha, c)));
               ob[k] = __fmul_rn(rstd[u], __fsub_rn(ub, __fmul_rn(xhb, c)));
-              wacc[sec][0][k] = __fadd_rn(wacc[sec][0][k], __fmul_rn(dpa[u][k], xha));
-              wacc[sec][1][k] = __fadd_rn(wacc[sec][1][k], __fmul_rn(dpb[u][k], xhb));
+              wacc[0][k] = __fadd_rn(wacc[0][k], __fmul_rn(dpa[u][k], xha));
+              wacc[1][k] = __fadd_rn(wacc[1][k], __fmul_rn(dpb[u][k], xhb));
             }
             st16(out + h * HD + 8 * l, pack8_rn(oa));
             st16(out + h * HD + HALF + 8 * l, pack8_rn(ob));
           }
+        }
+        // the token's sum for this section: stride tree over the lane groups
+        // (xor 16, then 8, ... down to L)
+#pragma unroll
+        for (int o = 16; o >= L; o >>= 1) {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) wacc[hf][k] = __fadd_rn(wacc[hf][k], __shfl_xor_sync(kFull, wacc[hf][k], o));
+        }
+        if (grp == 0) {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) xch[(warp * NSEC + sec) * HD + hf * HALF + 8 * l + k] = wacc[hf][k];
         }
         __syncwarp();  // the stage is read: refill it with unit u + nsw
         if (lane == 0 && unit_exists(u + nsw)) {
@@ -264,24 +274,8 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
         }
       }
     }
-    // token sum: stride tree over the lane groups (xor 16, then 8, ... down to L)
-#pragma unroll
-    for (int o = 16; o >= L; o >>= 1) {
-#pragma unroll
-      for (int sec = 0; sec < NSEC; ++sec)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            wacc[sec][hf][k] = __fadd_rn(wacc[sec][hf][k], __shfl_xor_sync(kFull, wacc[sec][hf][k], o));
-    }
-    if (grp == 0) {
-#pragma unroll
-      for (int sec = 0; sec < NSEC; ++sec)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-          for (int k = 0; k < 8; ++k) xch[(warp * NSEC + sec) * HD + hf * HALF + 8 * l + k] = wacc[sec][hf][k];
+    if (!has) {  // a token past the end (or a stopped warp) adds zeros
+      for (int i = lane; i < NSEC * HD; i += 32) xch[warp * NSEC * HD + i] = 0.0f;
     }
     __syncthreads();
     // chunk sum: stride tree over the warps (= tokens of the chunk)
@@ -313,12 +307,17 @@ static cudaError_t launch_headnorm_bwd(const HeadNormBwdArgs& a, int hd, cudaStr
   const size_t stage = 2 * static_cast<size_t>(a.heads) * hd * 2;  // one section: input + gradient
   const size_t fixed = static_cast<size_t>(kHnbWarps) * NSEC * hd * sizeof(float);
   const size_t per = kHnbWarps * (stage + sizeof(uint64_t));
-  int nsw = static_cast<int>((dev.max_smem_optin - fixed) / per);
+  // Two CTAs per SM (16 warps to hide the per-head dependency chains) with
+  // as many stages as then fit; one CTA with a deeper ring otherwise.
+  const size_t limit2 = kHnbCtaSmemFor2 > fixed ? kHnbCtaSmemFor2 - fixed : 0;
+  int ctas = limit2 >= per ? 2 : 1;
+  int nsw = static_cast<int>((ctas == 2 ? limit2 : dev.max_smem_optin - fixed) / per);
   if (nsw < 1) return cudaErrorInvalidValue;  // bounded by heads * head_dim <= 2048
   if (nsw > kHnbMaxStages) nsw = kHnbMaxStages;
   const size_t smem = fixed + per * nsw;
   const int64_t chunks = hn_chunks(a.tokens);
-  const dim3 grid(static_cast<unsigned>(chunks < dev.sms ? chunks : dev.sms));
+  const int64_t cap = static_cast<int64_t>(dev.sms) * ctas;
+  const dim3 grid(static_cast<unsigned>(chunks < cap ? chunks : cap));
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e = ensure_smem(kern, smem, true);
     if (e != cudaSuccess) return e;
