@@ -1,8 +1,8 @@
 """Generate golden vectors by running the reference's own Triton kernels.
 
-    python tests/golden/gen_golden.py [--reference PATH]
+    python tests/golden/gen_golden.py --reference PATH
 
-Imports tan0210/anima-flat's src/kernels (default PATH /root/reference, read
+Imports tan0210/anima-flat's src/kernels from the checkout at PATH (read
 only) with TRITON_INTERPRET=1, launches each hot-path kernel through its
 JITFunction (``kernel.fn[grid](...)``, bypassing the GPU-only autotuner) on
 small seeded CPU inputs, and writes the inputs and outputs to
@@ -37,7 +37,7 @@ def bits(t):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of tan0210/anima-flat (read only)")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, args.reference)
