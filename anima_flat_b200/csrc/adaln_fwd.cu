@@ -57,8 +57,9 @@ constexpr int kAdalnPairs = 8;
 constexpr int kAdalnWarps = 2 * kAdalnPairs;
 // Stages per pair.  A short launch (few rows per SM: config 2 has 27.7) is
 // mostly ramp and tail, and more stages delay each pair's first row behind the
-// others' copies, so it takes two (adaln too, whose 4 KiB stages would allow
-// more: three and four measured slower).  A long launch is a steady stream, where the
+// others' copies, so it takes two (measured: adaln, whose 4 KiB stages would
+// allow more, is slower with three or four; residual_adaln_fp8 at config 3
+// takes 33.8 µs with three, 26.5 with two).  A long launch is a steady stream, where the
 // bytes in flight bound the bandwidth, so it takes the deepest ring that fits,
 // giving up the shared-memory modulation slots if that buys a stage.
 constexpr int kAdalnShortStages = 2;
