@@ -147,8 +147,22 @@ adaln_bwd_stats_kernel(const AdalnStatsArgs a, const int use_smods) {
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) zf[i][jj] = bf2f2(word(zv, jj));
     }
-    const float mean = div_d(pair_canonical_sum2<NH, SPLIT>([&](int i, int jj) { return zf[i][jj]; }, xch,
-                                                             h, lane, bar_id));
+    // dxh = gh * scale (fp32 pairs)
+    f2_t dxh[NH][4];
+#pragma unroll
+    for (int i = 0; i < NH; ++i) {
+      const uint4 scv = !ok(i) ? make_uint4(0, 0, 0, 0)
+                        : smods ? lds16(mods + static_cast<size_t>(b - b_lo) * row_bytes + col(i) * 2)
+                                : ld_keep(a.scale + b * D + col(i));
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) dxh[i][jj] = mul2_noc(bf2f2(word(gv[i], jj)), bf2f2(word(scv, jj)));
+    }
+    // Round 1: sum(z) and sum(dxh), which need nothing else.
+    float mean, c1;
+    pair_canonical_sum2x2<NH, SPLIT>([&](int n, int i, int jj) { return n == 0 ? zf[i][jj] : dxh[i][jj]; }, xch, h,
+                                     lane, bar_id, mean, c1);
+    mean = div_d(mean);
+    c1 = div_d(c1);
     if (!SPLIT) named_bar_sync(bar_id, 64);
     if (leader && !dead && row_of(j + kStatStages) < r1) {  // both warps have read the stage
       fence_proxy_async_smem();
@@ -160,27 +174,13 @@ adaln_bwd_stats_kernel(const AdalnStatsArgs a, const int use_smods) {
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) zf[i][jj] = ok(i) ? sub2(zf[i][jj], mm) : 0ull;  // d = z - mean
     }
-    const float rstd = canonical_rstd(
-        div_d(pair_canonical_sum2<NH, SPLIT>([&](int i, int jj) { return mul2_noc(zf[i][jj], zf[i][jj]); },
-                                            xch + 2 * 4 * 32, h, lane, bar_id)),
-        a.eps);
-    const f2_t rr = f2(rstd, rstd);
-    // dxh = gh * scale (kept in gv's place as fp32 pairs); xhat = d * rstd
-    f2_t dxh[NH][4];
-#pragma unroll
-    for (int i = 0; i < NH; ++i) {
-      const uint4 scv = !ok(i) ? make_uint4(0, 0, 0, 0)
-                        : smods ? lds16(mods + static_cast<size_t>(b - b_lo) * row_bytes + col(i) * 2)
-                                : ld_keep(a.scale + b * D + col(i));
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) dxh[i][jj] = mul2_noc(bf2f2(word(gv[i], jj)), bf2f2(word(scv, jj)));
-    }
-    float c1, c2;
+    // Round 2: sum(d * d) and sum(dxh * d); c2 = (sum(dxh * d) * rstd) / D.
+    float var, e;
     pair_canonical_sum2x2<NH, SPLIT>(
-        [&](int n, int i, int jj) { return n == 0 ? dxh[i][jj] : mul2_noc(dxh[i][jj], mul2(zf[i][jj], rr)); },
-        xch + 2 * 2 * 4 * 32, h, lane, bar_id, c1, c2);
-    c1 = div_d(c1);
-    c2 = div_d(c2);
+        [&](int n, int i, int jj) { return mul2_noc(n == 0 ? zf[i][jj] : dxh[i][jj], zf[i][jj]); },
+        xch + 2 * 2 * 4 * 32, h, lane, bar_id, var, e);
+    const float rstd = canonical_rstd(div_d(var), a.eps);
+    const float c2 = div_d(__fmul_rn(e, rstd));
     if (leader && !dead) a.stats[row] = make_float4(mean, rstd, c1, c2);
   }
   if (leader && dead) {

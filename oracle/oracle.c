@@ -550,7 +550,10 @@ static void stride_tree_rows(const float* rows, int64_t n, int64_t cols, float* 
   free(t);
 }
 /* src/kernels/adaln.py:133-217.  Per row: mean, rstd of z; xhat = d*rstd;
- * dxh = gh*scale; c1 = sum(dxh)/D; c2 = sum(dxh*xhat)/D;
+ * dxh = gh*scale; c1 = sum(dxh)/D; c2 = sum(dxh*xhat)/D, which the canonical
+ * (RNE) mode forms as (sum(dxh*d) * rstd) / D: the same value up to
+ * rounding, with a sum that needs only the mean, so the device computes it
+ * together with the variance (INTERP mode keeps the reference's form);
  * dz = rstd*((dxh - c1) - xhat*c2) (+ gz) -> bf16; dx = bf16(dz*gate).
  * Parameter gradients (dshift = sum gh, dscale = sum gh*xhat,
  * dgate = sum dz*x) in the canonical order of the CUDA kernel: chunks of
@@ -594,10 +597,11 @@ void orc_adaln_bwd(const uint16_t* gh, const uint16_t* gz, const uint16_t* z, co
             const float xhat = (zf[i] - mean) * rstd;
             const float dxh = orc_bf16_to_f32(gh[o + i]) * orc_bf16_to_f32(scale[po + i]);
             t1[i] = dxh;
-            t2[i] = dxh * xhat;
+            t2[i] = mode == ROUND_INTERP ? dxh * xhat : dxh * (zf[i] - mean);
           }
           const float c1 = row_sum(t1, D, 32, mode) / (float)D;
-          const float c2 = row_sum(t2, D, 32, mode) / (float)D;
+          const float c2 = mode == ROUND_INTERP ? row_sum(t2, D, 32, mode) / (float)D
+                                                : (row_sum(t2, D, 32, mode) * rstd) / (float)D;
           float* p = wp + (int64_t)w * nq * D;
           for (int64_t i = 0; i < D; ++i) {
             const float g = orc_bf16_to_f32(gh[o + i]);
