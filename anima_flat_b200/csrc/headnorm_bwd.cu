@@ -9,6 +9,8 @@
 //   rstd = 1 / sqrt(sum(x*x) / hd + eps);  xhat = x * rstd;  u = d' * w
 //   c = sum(u * xhat) / hd;  dx = bf16(rstd * (u - xhat * c))
 //   dw += d' * xhat   (fp32, per dim)
+// c is formed as (sum(u * x) * rstd) / hd: the same value up to rounding, with
+// a sum that does not wait for rstd, so both head sums share one butterfly.
 // v's gradient is copied into the v third of dqkv (rope.py:304-326).
 //
 // Layout: persistent CTAs of kHnbWarps warps walk fixed chunks of kHnbWarps
@@ -168,7 +170,7 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
         for (int it0 = 0; it0 < iters; it0 += kHnbUnroll) {
           uint4 xa[kHnbUnroll], xb[kHnbUnroll];
           float dpa[kHnbUnroll][8], dpb[kHnbUnroll][8];  // rotated-back gradient
-          float ss[kHnbUnroll];
+          float ss[kHnbUnroll], cc[kHnbUnroll];  // sum(x * x), sum((d' * w) * x)
 #pragma unroll
           for (int u = 0; u < kHnbUnroll; ++u) {
             const int h = (it0 + u) * HPI + grp;
@@ -193,42 +195,34 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
             }
             unpack8(xa[u], fa);
             unpack8(xb[u], fb);
+            float ta[8], tb[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
+              ta[k] = __fmul_rn(__fmul_rn(dpa[u][k], w[0][k]), fa[k]);
+              tb[k] = __fmul_rn(__fmul_rn(dpb[u][k], w[1][k]), fb[k]);
               fa[k] = __fmul_rn(fa[k], fa[k]);
               fb[k] = __fmul_rn(fb[k], fb[k]);
             }
             ss[u] = __fadd_rn(vec_sum8(fa), vec_sum8(fb));
-          }
-#pragma unroll
-          for (int o = L / 2; o >= 1; o >>= 1) {
-#pragma unroll
-            for (int u = 0; u < kHnbUnroll; ++u) ss[u] = __fadd_rn(ss[u], __shfl_xor_sync(kFull, ss[u], o));
-          }
-          float rstd[kHnbUnroll], cc[kHnbUnroll];
-#pragma unroll
-          for (int u = 0; u < kHnbUnroll; ++u) {
-            rstd[u] = canonical_rstd(__fmul_rn(ss[u], 1.0f / HD), a.eps);
-            float fa[8], fb[8], ta[8], tb[8];
-            unpack8(xa[u], fa);
-            unpack8(xb[u], fb);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              ta[k] = __fmul_rn(__fmul_rn(dpa[u][k], w[0][k]), __fmul_rn(fa[k], rstd[u]));
-              tb[k] = __fmul_rn(__fmul_rn(dpb[u][k], w[1][k]), __fmul_rn(fb[k], rstd[u]));
-            }
             cc[u] = __fadd_rn(vec_sum8(ta), vec_sum8(tb));
           }
+          // Both head sums in one butterfly: c = (sum((d' * w) * x) * rstd) / HD.
 #pragma unroll
           for (int o = L / 2; o >= 1; o >>= 1) {
 #pragma unroll
-            for (int u = 0; u < kHnbUnroll; ++u) cc[u] = __fadd_rn(cc[u], __shfl_xor_sync(kFull, cc[u], o));
+            for (int u = 0; u < kHnbUnroll; ++u) {
+              ss[u] = __fadd_rn(ss[u], __shfl_xor_sync(kFull, ss[u], o));
+              cc[u] = __fadd_rn(cc[u], __shfl_xor_sync(kFull, cc[u], o));
+            }
           }
+          float rstd[kHnbUnroll];
+#pragma unroll
+          for (int u = 0; u < kHnbUnroll; ++u) rstd[u] = canonical_rstd(__fmul_rn(ss[u], 1.0f / HD), a.eps);
 #pragma unroll
           for (int u = 0; u < kHnbUnroll; ++u) {
             const int h = (it0 + u) * HPI + grp;
             if (it0 + u >= iters || h >= H) continue;
-            const float c = __fmul_rn(cc[u], 1.0f / HD);
+            const float c = __fmul_rn(__fmul_rn(cc[u], rstd[u]), 1.0f / HD);
             float fa[8], fb[8], oa[8], ob[8];
             unpack8(xa[u], fa);
             unpack8(xb[u], fb);

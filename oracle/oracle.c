@@ -639,6 +639,9 @@ void orc_adaln_bwd(const uint16_t* gh, const uint16_t* gz, const uint16_t* z, co
  * rotation of the upstream gradient (da' = da*cos + db*sin,
  * db' = db*cos - da*sin), rstd of the forward input, xhat = x*rstd,
  * u = d'*w, c = sum(u*xhat)/hd, dx = bf16(rstd*(u - xhat*c)); dw += d'*xhat.
+ * The canonical (RNE) mode forms c as (sum(u*x) * rstd)/hd: the same value
+ * up to rounding, from a sum that needs no rstd, so the device reduces it
+ * together with sum(x*x) (INTERP mode keeps the reference's form).
  * Weight-gradient order as the CUDA kernel: tokens in chunks of `warps`;
  * per token, lane group g (hpi = 32 / (hd/16) groups) sums heads
  * g, g + hpi, ... in increasing order from zero and the groups combine as a
@@ -691,10 +694,14 @@ void orc_headnorm_bwd(const uint16_t* src, int64_t src_row, int64_t q_off, int64
                                  ? orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)
                                  : orc_canonical_sum(t, hd, (int)(hd / 8));
             const float rstd = 1.0f / sqrtf(ss / (float)hd + eps);
-            for (int64_t i = 0; i < hd; ++i) t[i] = (d[i] * wv[i]) * (x[i] * rstd);
-            const float cc = ((mode == ROUND_INTERP)
-                                  ? orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)
-                                  : orc_canonical_sum(t, hd, (int)(hd / 8))) / (float)hd;
+            float cc;
+            if (mode == ROUND_INTERP) {
+              for (int64_t i = 0; i < hd; ++i) t[i] = (d[i] * wv[i]) * (x[i] * rstd);
+              cc = (orc_numpy_sum(t, half) + orc_numpy_sum(t + half, half)) / (float)hd;
+            } else {
+              for (int64_t i = 0; i < hd; ++i) t[i] = (d[i] * wv[i]) * x[i];
+              cc = (orc_canonical_sum(t, hd, (int)(hd / 8)) * rstd) / (float)hd;
+            }
             for (int64_t i = 0; i < hd; ++i) {
               const float xh = x[i] * rstd, u = d[i] * wv[i];
               out[h * hd + i] = orc_f32_to_bf16(rstd * (u - xh * cc), mode);
