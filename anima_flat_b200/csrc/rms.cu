@@ -371,8 +371,10 @@ rms_bwd_kernel(const RmsArgs a) {
           for (int e = 0; e < 4; ++e) {
             n2[e] = mul2(f2(sv[2 * e], sv[2 * e + 1]), rr);
             av2[e] = mul2(n2[e], f2(gv[2 * e], gv[2 * e + 1]));
+            // Out of the core's range the pair's values are meaningless (the
+            // SFU and integer steps cannot fault) and are redone below.
             const bool in = fmaxf(fabsf(f2lo(av2[e])), fabsf(f2hi(av2[e]))) <= 87.0f;
-            sg2[e] = sigmoid_core2(in ? av2[e] : f2_t{0});
+            sg2[e] = sigmoid_core2(av2[e]);
             if (!in) out |= 1u << e;
           }
           if (__any_sync(kFull, out != 0)) {
