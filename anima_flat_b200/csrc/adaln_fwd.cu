@@ -10,9 +10,9 @@
 //   bf16 output:  h = bf16(y)
 //   FP8 output:   s = max(max|y|, 1e-12) / 448;  q = e4m3(clamp(y / s, +-448))
 //
-// Layout: persistent CTAs, one per SM, of kAdalnPairs warp pairs.  CTA c owns
+// Layout: persistent CTAs, one per SM, of P warp pairs.  CTA c owns
 // the contiguous rows [c*R/G, (c+1)*R/G) (R rows, G CTAs: every SM gets the
-// same share within one row), and pair p of it the rows p, p + kAdalnPairs, ...
+// same share within one row), and pair p of it the rows p, p + P, ...
 // of that range.  Each pair keeps a private ring of `nsw` shared-memory stages;
 // its leader lane streams each row's res (and x) into a stage with bulk copies
 // (TMA engine) that complete on the stage's mbarrier, so up to nsw rows per
@@ -53,8 +53,13 @@ struct AdalnArgs {
   float eps;
 };
 
+// Warp pairs per CTA.  The FP8 kernels at D = 2048 are bound by the latency
+// of each row's chain of sums and run 12 pairs (80 registers, no spills; 24
+// warps per SM): measured 4-5% faster than 8 pairs in short launches, though
+// their row stage ring then has one stage.  Every other instantiation runs 8
+// pairs (up to 128 registers); 12 pairs made plain adaln slower.
 constexpr int kAdalnPairs = 8;
-constexpr int kAdalnWarps = 2 * kAdalnPairs;
+constexpr int kAdalnPairsFp8 = 12;
 // Stages per pair.  A short launch (few rows per SM: config 2 has 27.7) is
 // mostly ramp and tail, and more stages delay each pair's first row behind the
 // others' copies, so it takes two (measured: adaln, whose 4 KiB stages would
@@ -83,8 +88,8 @@ __host__ __device__ constexpr size_t adaln_mod_bytes(int64_t dim, bool has_x) {
 
 // EXACT: dim == 256 * NC, so every lane owns NC full vectors (no masking).
 // use_smods: the launch reserved shared memory for the modulation slots.
-template <int NC, bool HAS_X, bool FP8, bool EXACT>
-__global__ void __launch_bounds__(kAdalnWarps * 32, 1)
+template <int P, int NC, bool HAS_X, bool FP8, bool EXACT>
+__global__ void __launch_bounds__(P * 64, 1)
 adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const int early) {
   // SPLIT: the pair divides each lane's vectors; for NC == 1 both warps hold
   // the single vector and warp 0 writes the outputs.
@@ -102,15 +107,15 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
   const uint32_t row_bytes = static_cast<uint32_t>(D) * 2u;
   const uint32_t stage_bytes = (HAS_X ? 2u : 1u) * row_bytes;
   const size_t slot_bytes = adaln_slot_bytes(D, HAS_X);
-  const size_t ring_all = static_cast<size_t>(kAdalnPairs) * nsw * stage_bytes;
+  const size_t ring_all = static_cast<size_t>(P) * nsw * stage_bytes;
   uint8_t* ring = smem + static_cast<size_t>(pair) * nsw * stage_bytes;
   uint8_t* xbase = smem + ring_all + static_cast<size_t>(pair) * kAdalnPairXchBytes;
   f2_t* xch = reinterpret_cast<f2_t*>(xbase);
   float* xmax = reinterpret_cast<float*>(xbase + kAdalnXchF2 * sizeof(f2_t));
-  uint8_t* mods = smem + ring_all + kAdalnPairs * kAdalnPairXchBytes;
+  uint8_t* mods = smem + ring_all + P * kAdalnPairXchBytes;
   uint64_t* bars0 = reinterpret_cast<uint64_t*>(mods + (use_smods ? adaln_mod_bytes(D, HAS_X) : 0));
   uint64_t* bars = bars0 + pair * nsw;
-  uint64_t* modbar = bars0 + kAdalnPairs * nsw;
+  uint64_t* modbar = bars0 + P * nsw;
 
   // This CTA's rows, and the batch entries they belong to.
   const int64_t r0 = a.rows * blockIdx.x / gridDim.x;
@@ -140,7 +145,7 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
   }
   if (smods) __syncthreads();
 
-  auto row_of = [&](int64_t j) { return r0 + pair + j * kAdalnPairs; };
+  auto row_of = [&](int64_t j) { return r0 + pair + j * P; };
   auto issue = [&](int64_t j) {  // leader: stream row row_of(j) into stage j % nsw
     const int64_t row = row_of(j);
     const int s = static_cast<int>(j % nsw);
@@ -300,9 +305,19 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
       }
       const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
       const float rc = __fdiv_rn(1.0f, sc);
+      // Every vector's bracketed codes first (independent chains), then one
+      // branch for the rare open pair.
+      uint2 code[NH];
+      bool settled = true;
+#pragma unroll
+      for (int i = 0; i < NH; ++i) code[i] = e4m3_try8(y[i], rc, settled);
+      if (!settled) {
+#pragma unroll
+        for (int i = 0; i < NH; ++i) code[i] = e4m3_ieee8(y[i], sc);
+      }
 #pragma unroll
       for (int i = 0; i < NH; ++i) {
-        if (ok(i) && store) st8(a.q + base + col(i), e4m3_quot8(y[i], sc, rc));
+        if (ok(i) && store) st8(a.q + base + col(i), code[i]);
       }
       if (leader && !dead) a.s[row] = sc;
     }
@@ -323,9 +338,9 @@ struct AdalnPlan {
   int early;  // refill a stage right after the pair has read it (one more pair barrier per row)
   size_t smem;
 };
-static AdalnPlan adaln_plan(int64_t dim, bool has_x, size_t limit, bool long_launch) {
-  const size_t per = kAdalnPairs * ((has_x ? 2 : 1) * static_cast<size_t>(dim) * 2 + sizeof(uint64_t));
-  const size_t xch = kAdalnPairs * kAdalnPairXchBytes + sizeof(uint64_t);
+static AdalnPlan adaln_plan(int64_t dim, bool has_x, size_t limit, bool long_launch, int pairs) {
+  const size_t per = pairs * ((has_x ? 2 : 1) * static_cast<size_t>(dim) * 2 + sizeof(uint64_t));
+  const size_t xch = pairs * kAdalnPairXchBytes + sizeof(uint64_t);
   const size_t mods = adaln_mod_bytes(dim, has_x);
   const int cap = long_launch ? kAdalnMaxStages : kAdalnShortStages;
   auto stages = [&](size_t fixed) {
@@ -347,19 +362,31 @@ static cudaError_t launch_adaln(const AdalnArgs& a, cudaStream_t st) {
   if (dev.error != cudaSuccess) return dev.error;
   const int nc = row_chunks(a.dim);
   const bool exact = a.dim == 256 * nc;
-  const int64_t want = (a.rows + kAdalnPairs - 1) / kAdalnPairs;
-  const dim3 grid(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
-  const AdalnPlan plan = adaln_plan(a.dim, HAS_X, dev.max_smem_optin,
-                                    a.rows >= kAdalnLongRowsPerCta * static_cast<int64_t>(grid.x));
-  const dim3 block(kAdalnWarps * 32);
-  auto go = [&](auto kern) -> cudaError_t {
+  auto plan_for = [&](int pairs, dim3& grid) {
+    const int64_t want = (a.rows + pairs - 1) / pairs;
+    grid = dim3(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
+    return adaln_plan(a.dim, HAS_X, dev.max_smem_optin, a.rows >= kAdalnLongRowsPerCta * static_cast<int64_t>(grid.x),
+                      pairs);
+  };
+  auto go = [&](auto kern, int pairs, const dim3& grid, const AdalnPlan& plan) -> cudaError_t {
     cudaError_t e = ensure_smem(kern, plan.smem);
     if (e != cudaSuccess) return e;
-    return launch_pdl(kern, grid, block, plan.smem, st, a, plan.nsw, plan.smods, plan.early);
+    return launch_pdl(kern, grid, dim3(pairs * 64), plan.smem, st, a, plan.nsw, plan.smods, plan.early);
   };
-#define AFB_LAUNCH_ADALN(NC)                                            \
-  return exact ? go(adaln_fwd_kernel<NC, HAS_X, FP8, true>) \
-               : go(adaln_fwd_kernel<NC, HAS_X, FP8, false>)
+  dim3 grid;
+  if constexpr (FP8) {
+    if (exact && nc == 8) {
+      // The 12-pair kernel for short launches whose stage fits (see kAdalnPairsFp8).
+      const AdalnPlan p12 = plan_for(kAdalnPairsFp8, grid);
+      const bool fits = p12.smem <= dev.max_smem_optin;
+      if (fits && a.rows < kAdalnLongRowsPerCta * static_cast<int64_t>(grid.x))
+        return go(adaln_fwd_kernel<kAdalnPairsFp8, 8, HAS_X, true, true>, kAdalnPairsFp8, grid, p12);
+    }
+  }
+  const AdalnPlan plan = plan_for(kAdalnPairs, grid);
+#define AFB_LAUNCH_ADALN(NC)                                                                     \
+  return exact ? go(adaln_fwd_kernel<kAdalnPairs, NC, HAS_X, FP8, true>, kAdalnPairs, grid, plan) \
+               : go(adaln_fwd_kernel<kAdalnPairs, NC, HAS_X, FP8, false>, kAdalnPairs, grid, plan)
   switch (nc) {
     case 1: AFB_LAUNCH_ADALN(1);
     case 2: AFB_LAUNCH_ADALN(2);

@@ -325,10 +325,13 @@ __device__ __forceinline__ uint32_t f2bf2(f2_t v) { return pack2_rn(f2lo(v), f2h
 // clamped, so a NaN quotient (clamped to -448 by the reference) never
 // matches and takes the exact path.  Where any pair of the vector is open,
 // all eight codes come from the IEEE quotient.
-__device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, float r) {
+//
+// e4m3_try8 forms the bracketed codes and clears `settled` where a pair is
+// open, with no branch, so a kernel can form every vector's codes first and
+// take one (rare) branch to e4m3_ieee8 after them all.
+__device__ __forceinline__ uint2 e4m3_try8(const float (&y)[8], float r, bool& settled) {
   const f2_t rr = f2(r, r);
   uint32_t hi[4];
-  bool settled = true;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const f2_t q = mul2(f2(y[2 * j], y[2 * j + 1]), rr);
@@ -337,13 +340,18 @@ __device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, float 
     hi[j] = e4m3x2(f2lo(b), f2hi(b));
     settled = settled && e4m3x2(clamp448(f2lo(a)), clamp448(f2hi(a))) == hi[j];
   }
-  if (!settled) {
-    float q[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) q[k] = clamp448(__fdiv_rn(y[k], s));
-    return e4m3x8(q);
-  }
   return make_uint2(hi[0] | (hi[1] << 16), hi[2] | (hi[3] << 16));
+}
+__device__ __forceinline__ uint2 e4m3_ieee8(const float (&y)[8], float s) {
+  float q[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) q[k] = clamp448(__fdiv_rn(y[k], s));
+  return e4m3x8(q);
+}
+__device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, float r) {
+  bool settled = true;
+  const uint2 c = e4m3_try8(y, r, settled);
+  return settled ? c : e4m3_ieee8(y, s);
 }
 
 // Element-wise scalar products of two pairs, kept scalar so that they are never

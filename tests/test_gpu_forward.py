@@ -46,7 +46,9 @@ def dev(a, cuda_dev):
 # entries read the modulation from global memory instead of shared memory.
 # (3, 8192, 512) and (5, 4096, 2048): long launches (>= 128 rows per CTA),
 # which take the deep ring; at D = 2048 the residual one gives up the
-# shared-memory modulation slots for it.
+# shared-memory modulation slots for it.  The FP8 kernels at D = 2048 run 12
+# warp pairs per CTA in short launches ((2, 4096, 2048), (64, 1, 2048)) and 8
+# in long ones ((5, 4096, 2048)).
 ADALN_SHAPES = [(1, 1, 2048), (2, 3, 2048), (1, 4096, 2048), (2, 37, 1024), (3, 5, 256),
                 (1, 7, 4096), (1, 9, 8), (2, 11, 2040), (1, 3, 520), (64, 1, 2048), (40, 3, 1024),
                 (3, 8192, 512), (5, 4096, 2048)]
@@ -75,7 +77,7 @@ def test_adaln_bit_exact(B, S, D, cuda_dev):
 
 @pytest.mark.parametrize("B,S,D", [(1, 1, 2048), (2, 4096, 2048), (2, 37, 1024), (3, 5, 256),
                                    (1, 7, 4096), (2, 11, 2040), (64, 1, 2048), (40, 3, 1024),
-                                   (3, 8192, 512)])
+                                   (3, 8192, 512), (5, 4096, 2048)])
 @pytest.mark.parametrize("has_x", [True, False])
 def test_adaln_fp8_bit_exact(B, S, D, has_x, cuda_dev):
     r = rng(B * 3000 + S + D + has_x)
