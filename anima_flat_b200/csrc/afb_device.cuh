@@ -600,26 +600,27 @@ __device__ __forceinline__ float canonical_gelu(float x) {
 
 // The same formula on the special-function unit (rcp.approx, ex2.approx).
 // It keeps the canonical formula's rounding structure where it matters: the
-// erfc term is subtracted from 1 with one rounding (y = RN(1 - p*e)) and
-// gelu = (x/2) * (1 +- y), so for x < 0, where 1 - y cancels, the fast value
-// sits on the same 2^-24 grid as the canonical one.  1/sqrt2 is folded into
-// the constants of t and of the exponent.  Absolute error stays below
+// erfc term is subtracted from 1 with one rounding (y = RN(1 - p*e)), and
+// gelu = (x/2) * (1 +- y) is one FMA, RN(|x|/2 * y + x/2): for x < 0, where
+// 1 - y cancels, that is RN((x/2) * (1 - y)) exactly as in the canonical
+// formula, and for x >= 0 it skips the rounding of 1 + y.  1/sqrt2 is folded
+// into the constants of t and of the exponent.  Absolute error stays below
 // 2^-20 + 2^-12 * |gelu(x)|; the row kernel uses it for the codes and
 // recomputes the canonical value for amax candidates.
 __device__ __forceinline__ float fast_gelu(float x) {
+  const float hx = 0.5f * x, hax = 0.5f * fabsf(x);
   float t;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(__fmaf_rn(fabsf(x), 0.3275911f * 0.707106769084930419921875f, 1.0f)));
-  float p = __fmaf_rn(1.061405429f, t, -1.453152027f);
-  p = __fmaf_rn(p, t, 1.421413741f);
-  p = __fmaf_rn(p, t, -0.284496736f);
-  p = __fmaf_rn(p, t, 0.254829592f);
-  p = p * t;
+  // hax * 2c == |x| * c exactly (a power-of-two scaling)
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(__fmaf_rn(hax, 2.0f * (0.3275911f * 0.707106769084930419921875f), 1.0f)));
+  float n = __fmaf_rn(-1.061405429f, t, 1.453152027f);  // n = -p (see fast_gelu2)
+  n = __fmaf_rn(n, t, -1.421413741f);
+  n = __fmaf_rn(n, t, 0.284496736f);
+  n = __fmaf_rn(n, t, -0.254829592f);
+  n = n * t;
   float e;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"((x * x) * -0.721347520444481703680f));
-  const float y = __fmaf_rn(-p, e, 1.0f);
-  // (x/2) * (1 +- y) == x * (1/2 +- y/2): halving is exact, so one FMA forms
-  // the same rounded factor.
-  return x * __fmaf_rn(0.5f, copysignf(y, x), 0.5f);
+  const float y = __fmaf_rn(n, e, 1.0f);
+  return __fmaf_rn(hax, y, hx);
 }
 
 // fast_gelu on a pair of elements with packed fp32x2 arithmetic: the same
@@ -634,23 +635,27 @@ __device__ __forceinline__ f2_t fma2(f2_t a, f2_t b, f2_t c) {
 }
 __device__ __forceinline__ f2_t splat2(float v) { return f2(v, v); }
 __device__ __forceinline__ f2_t fast_gelu2(f2_t x) {
-  constexpr f2_t kAbs = 0x7fffffff7fffffffull, kSign = 0x8000000080000000ull;
-  const f2_t den = fma2(x & kAbs, splat2(0.3275911f * 0.707106769084930419921875f), splat2(1.0f));
+  constexpr f2_t kAbs = 0x7fffffff7fffffffull;
+  const f2_t hx = mul2(x, splat2(0.5f));
+  const f2_t hax = mul2(x & kAbs, splat2(0.5f));
+  const f2_t den = fma2(hax, splat2(2.0f * (0.3275911f * 0.707106769084930419921875f)), splat2(1.0f));
   float t0, t1;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(f2lo(den)));
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(f2hi(den)));
   const f2_t t = f2(t0, t1);
-  f2_t p = fma2(splat2(1.061405429f), t, splat2(-1.453152027f));
-  p = fma2(p, t, splat2(1.421413741f));
-  p = fma2(p, t, splat2(-0.284496736f));
-  p = fma2(p, t, splat2(0.254829592f));
-  p = mul2(p, t);
+  // n = -p, from the negated coefficients: RN(-v) = -RN(v), so every step
+  // is the exact negation of the canonical order's, and 1 - p*e = fma(n, e, 1).
+  f2_t n = fma2(splat2(-1.061405429f), t, splat2(1.453152027f));
+  n = fma2(n, t, splat2(-1.421413741f));
+  n = fma2(n, t, splat2(0.284496736f));
+  n = fma2(n, t, splat2(-0.254829592f));
+  n = mul2(n, t);
   const f2_t arg = mul2(mul2(x, x), splat2(-0.721347520444481703680f));
   float e0, e1;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(f2lo(arg)));
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(f2hi(arg)));
-  const f2_t y = fma2(p ^ kSign, f2(e0, e1), splat2(1.0f));  // 1 - p*e
-  return mul2(x, fma2(splat2(0.5f), (y & kAbs) | (x & kSign), splat2(0.5f)));  // copysign(y, x)
+  const f2_t y = fma2(n, f2(e0, e1), splat2(1.0f));  // 1 - p*e
+  return fma2(hax, y, hx);
 }
 
 // The trimmed cross-attention's gain (src/kernels/ctx_scale.py:8-37):
