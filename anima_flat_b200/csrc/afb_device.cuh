@@ -719,30 +719,34 @@ __device__ __forceinline__ uint32_t silu_pair_bf16(f2_t a, f2_t v, bool& settled
 // form: r = 1 - d * y (exact), y + y * r.
 __device__ __forceinline__ f2_t sigmoid_core2(f2_t a) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr f2_t kSign = 0x8000000080000000ull;
-  const f2_t x = a ^ kSign;              // canonical_sigmoid takes exp(-a)
-  const float t0 = __fadd_rn(__fmul_rn(f2lo(x), 1.44269502162933349609375f), kRound);
-  const float t1 = __fadd_rn(__fmul_rn(f2hi(x), 1.44269502162933349609375f), kRound);
+  // canonical_sigmoid takes exp(x) at x = -a.  The sign is carried by the
+  // constants instead (RN(-v) = -RN(v)): the product x * log2e is a times
+  // -log2e; m = -r is the reduction applied to a; and the polynomial in
+  // r = -m runs as n1 = -p1, p2, n3 = -p3, ..., n7 = -p7 with every other
+  // constant negated, so e' = n7 * 2^k = -e and d = 1 + e = 1 - e'.
+  const float t0 = __fadd_rn(__fmul_rn(f2lo(a), -1.44269502162933349609375f), kRound);
+  const float t1 = __fadd_rn(__fmul_rn(f2hi(a), -1.44269502162933349609375f), kRound);
   const f2_t k = sub2(f2(t0, t1), splat2(kRound));
-  f2_t r = fma2(k, splat2(-0.693145751953125f), x);
-  r = fma2(k, splat2(-1.428606765330187e-06f), r);
-  f2_t p = fma2(splat2(1.98412701138295233249664306640625e-04f), r,
-                splat2(1.38888892251998186111450195312500e-03f));
-  p = fma2(p, r, splat2(8.33333376795053482055664062500000e-03f));
-  p = fma2(p, r, splat2(4.16666679084300994873046875000000e-02f));
-  p = fma2(p, r, splat2(1.66666671633720397949218750000000e-01f));
-  p = fma2(p, r, splat2(0.5f));
-  p = fma2(p, r, splat2(1.0f));
-  p = fma2(p, r, splat2(1.0f));
+  f2_t m = fma2(k, splat2(0.693145751953125f), a);
+  m = fma2(k, splat2(1.428606765330187e-06f), m);
+  f2_t p = fma2(splat2(1.98412701138295233249664306640625e-04f), m,
+                splat2(-1.38888892251998186111450195312500e-03f));
+  p = fma2(p, m, splat2(8.33333376795053482055664062500000e-03f));
+  p = fma2(p, m, splat2(-4.16666679084300994873046875000000e-02f));
+  p = fma2(p, m, splat2(1.66666671633720397949218750000000e-01f));
+  p = fma2(p, m, splat2(-0.5f));
+  p = fma2(p, m, splat2(1.0f));
+  p = fma2(p, m, splat2(-1.0f));
   // bits of t = 0x4B400000 + k; 2^k = (k + 127) << 23
   constexpr int kBias = 127 - 0x4B400000;
   const float e0 = __fmul_rn(f2lo(p), __int_as_float((__float_as_int(t0) + kBias) << 23));
   const float e1 = __fmul_rn(f2hi(p), __int_as_float((__float_as_int(t1) + kBias) << 23));
-  const float d0 = __fadd_rn(1.0f, e0), d1 = __fadd_rn(1.0f, e1);
+  const float d0 = __fsub_rn(1.0f, e0), d1 = __fsub_rn(1.0f, e1);
   float y0, y1;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(d0));
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y1) : "f"(d1));
   const f2_t d = f2(d0, d1), y = f2(y0, y1);
+  constexpr f2_t kSign = 0x8000000080000000ull;
   const f2_t rr = fma2(d ^ kSign, y, splat2(1.0f));
   return fma2(y, rr, y);
 }
