@@ -30,8 +30,9 @@
 // from registers.  z = res + gate*x uses packed bf16x2 arithmetic; the
 // statistics and the modulation use packed fp32x2 adds/subs under the
 // contraction rule of afb_device.cuh.  In FP8 mode y stays in registers
-// between the row max and the codes, and y / s is the product by RN(1/s)
-// wherever that provably gives the IEEE quotient's code (e4m3_quot8).
+// between the row max and the codes, and each code comes from products of y
+// by RN(1/s) (1 -+ 2^-22) wherever they provably give the IEEE quotient's
+// code (e4m3_try8).
 #include "afb_device.cuh"
 #include "afb_launch.h"
 
@@ -304,13 +305,13 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
         amax = fmaxf(xmax[0], xmax[1]);
       }
       const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
-      const float rc = __fdiv_rn(1.0f, sc);
+      const f2_t rb = e4m3_bracket(__fdiv_rn(1.0f, sc));
       // Every vector's bracketed codes first (independent chains), then one
       // branch for the rare open pair.
       uint2 code[NH];
       bool settled = true;
 #pragma unroll
-      for (int i = 0; i < NH; ++i) code[i] = e4m3_try8(y[i], rc, settled);
+      for (int i = 0; i < NH; ++i) code[i] = e4m3_try8(y[i], rb, settled);
       if (!settled) {
 #pragma unroll
         for (int i = 0; i < NH; ++i) code[i] = e4m3_ieee8(y[i], sc);

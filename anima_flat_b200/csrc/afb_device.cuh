@@ -317,26 +317,31 @@ __device__ __forceinline__ f2_t bf2f2(uint32_t w) { return f2(bf_lo(w), bf_hi(w)
 __device__ __forceinline__ uint32_t f2bf2(f2_t v) { return pack2_rn(f2lo(v), f2hi(v)); }
 
 // e4m3 codes of clamp(RN(y[k] / s), +-448).  r = RN(1/s) has relative error
-// at most 2^-24, so q = RN(y * r) lies within 1 ulp of the correctly rounded
-// quotient Q = RN(y / s).  Each pair converts q * (1 - 2^-22) and q * (1 + 2^-22),
-// at least 1.5 ulp below and above q after rounding, so Q lies between them;
-// e4m3 rounding (saturating) is monotone, so when both ends give the same
-// code, that is Q's code, and it is the result.  The lower end alone is
-// clamped, so a NaN quotient (clamped to -448 by the reference) never
-// matches and takes the exact path.  Where any pair of the vector is open,
-// all eight codes come from the IEEE quotient.
+// at most 2^-24, and rl = RN(r * (1 - 2^-22)), rh = RN(r * (1 + 2^-22)) two
+// more roundings of at most 2^-24 each, so as real numbers
+//   |y| * rl <= |y/s| (1 + 2^-24)^2 (1 - 2^-22) < |y/s|  and  |y| * rh > |y/s|.
+// RN is monotone, so RN(y * rl) and RN(y * rh) bracket the correctly
+// rounded quotient Q = RN(y / s) in magnitude; e4m3 rounding (saturating)
+// is monotone too, so when both ends give the same code, that is Q's code,
+// and it is the result.  The lower end alone is clamped, so a NaN quotient
+// (clamped to -448 by the reference) never matches and takes the exact
+// path.  Where any pair of the vector is open, all eight codes come from the
+// IEEE quotient.  e4m3_bracket gives (rl, rh) for r.
 //
 // e4m3_try8 forms the bracketed codes and clears `settled` where a pair is
 // open, with no branch, so a kernel can form every vector's codes first and
 // take one (rare) branch to e4m3_ieee8 after them all.
-__device__ __forceinline__ uint2 e4m3_try8(const float (&y)[8], float r, bool& settled) {
-  const f2_t rr = f2(r, r);
+__device__ __forceinline__ f2_t e4m3_bracket(float r) {
+  return f2(__fmul_rn(r, 1.0f - 0x1p-22f), __fmul_rn(r, 1.0f + 0x1p-22f));
+}
+__device__ __forceinline__ uint2 e4m3_try8(const float (&y)[8], f2_t rb, bool& settled) {
+  const f2_t rl = f2(f2lo(rb), f2lo(rb)), rh = f2(f2hi(rb), f2hi(rb));
   uint32_t hi[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const f2_t q = mul2(f2(y[2 * j], y[2 * j + 1]), rr);
-    const f2_t a = mul2(q, f2(1.0f - 0x1p-22f, 1.0f - 0x1p-22f));
-    const f2_t b = mul2(q, f2(1.0f + 0x1p-22f, 1.0f + 0x1p-22f));
+    const f2_t v = f2(y[2 * j], y[2 * j + 1]);
+    const f2_t a = mul2(v, rl);
+    const f2_t b = mul2(v, rh);
     hi[j] = e4m3x2(f2lo(b), f2hi(b));
     settled = settled && e4m3x2(clamp448(f2lo(a)), clamp448(f2hi(a))) == hi[j];
   }
@@ -348,9 +353,9 @@ __device__ __forceinline__ uint2 e4m3_ieee8(const float (&y)[8], float s) {
   for (int k = 0; k < 8; ++k) q[k] = clamp448(__fdiv_rn(y[k], s));
   return e4m3x8(q);
 }
-__device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, float r) {
+__device__ __forceinline__ uint2 e4m3_quot8(const float (&y)[8], float s, f2_t rb) {
   bool settled = true;
-  const uint2 c = e4m3_try8(y, r, settled);
+  const uint2 c = e4m3_try8(y, rb, settled);
   return settled ? c : e4m3_ieee8(y, s);
 }
 

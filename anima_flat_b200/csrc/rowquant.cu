@@ -13,10 +13,11 @@
 // with one barrier each.  The amax is a max, so the order of the reduction
 // does not matter.
 //
-// Without GELU the codes and scales are exact: q = y / s is the product by
-// RN(1/s) where that provably gives the code of the IEEE quotient, and the
-// IEEE division elsewhere (e4m3_quot8).  With GELU the per-element work would make the kernel
-// compute-bound, so the codes use fast_gelu() and y * (1 / s); the scale stays
+// Without GELU the codes and scales are exact: the codes come from products
+// of y by RN(1/s) (1 -+ 2^-22) where they provably bracket the IEEE quotient,
+// and from the IEEE division elsewhere (e4m3_quot8).  With GELU the
+// per-element work would make the kernel compute-bound, so the codes use
+// fast_gelu() and y * (1 / s); the scale stays
 // exact: every element whose fast value lies within the fast_gelu error bound
 // of the row's fast amax is recomputed with canonical_gelu() and the exact
 // amax is the max over those candidates.  The codes can then differ from the
@@ -146,6 +147,7 @@ rowquant_kernel(const RowquantArgs a) {
 
   const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
   const float r = __fdiv_rn(1.0f, s);
+  const f2_t rb = e4m3_bracket(r);
   if (!row_ok) return;
 #pragma unroll
   for (int c = 0; c < CPL; ++c) {
@@ -171,8 +173,8 @@ rowquant_kernel(const RowquantArgs a) {
           hi[2 * k] = f2lo(y2[c][k + 4]);
           hi[2 * k + 1] = f2hi(y2[c][k + 4]);
         }
-        plo = e4m3_quot8(lo, s, r);
-        phi = e4m3_quot8(hi, s, r);
+        plo = e4m3_quot8(lo, s, rb);
+        phi = e4m3_quot8(hi, s, rb);
       }
       st16(a.q + base + e, make_uint4(plo.x, plo.y, phi.x, phi.y));
     }
