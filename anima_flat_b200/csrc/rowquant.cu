@@ -56,8 +56,12 @@ struct RowquantArgs {
 
 __host__ __device__ constexpr int rowquant_block_warps(int group) { return group > 4 ? group : 4; }
 
+// The GELU kernel at K = 8192 (8 warps a row) asks for five CTAs per SM: 48
+// registers without spills, 40 warps per SM to cover the row's barrier
+// waits and SFU latency (measured 52.4 against 56.6 us with four CTAs of 64
+// registers; six CTAs spill and take 55.3).
 template <int CPL, int GROUP, bool GELU, bool CTX = false>
-__global__ void __launch_bounds__(rowquant_block_warps(GROUP) * 32)
+__global__ void __launch_bounds__(rowquant_block_warps(GROUP) * 32, (GELU && GROUP == 8) ? 5 : 1)
 rowquant_kernel(const RowquantArgs a) {
   constexpr int BW = rowquant_block_warps(GROUP);
   __shared__ float red[2][BW];
