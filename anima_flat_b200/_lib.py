@@ -29,6 +29,7 @@ SIGNATURES: dict[str, tuple] = {
     "afb_rowquant": (_P, _P, _P, _I, _I, c_int, _P),
     "afb_gelu_probe": (_P, _P, _P, _I, _P),
     "afb_silu_probe": (_P, _P),
+    "afb_wait_probe": (ctypes.c_uint32, _P, _P),
     "afb_qkv_norm_rope": (_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P),
     "afb_head_norm": (_P, _P, _P, _I, _I, _I, _I, _F, _P),
     "afb_residual_adaln_bwd": (_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _P,
@@ -90,6 +91,8 @@ def load() -> ctypes.CDLL:
     lib.afb_last_error.argtypes = []
     lib.afb_device_status.argtypes = [ctypes.POINTER(c_int)]
     lib.afb_device_status.restype = c_int
+    lib.afb_take_device_status.argtypes = [ctypes.POINTER(c_int)]
+    lib.afb_take_device_status.restype = c_int
     lib.afb_set_pdl.argtypes = [c_int]
     lib.afb_set_pdl.restype = None
     lib.afb_get_pdl.argtypes = []

@@ -12,23 +12,32 @@
 //   dshift[b] += gh;  dscale[b] += gh * xhat;  dgate[b] += dz * x   (fp32)
 //
 // Parameter-gradient order (deterministic, independent of the launch shape):
-// the rows of each batch entry are cut into chunks of kChunkRows = 16; in a
-// chunk, stream w (w < 4) sums rows w, w + 4, w + 8, w + 12 in increasing
-// order from zero; the four stream sums combine as a stride tree,
-// (p0 + p2) + (p1 + p3); the chunk sums combine by a stride tree over the
-// chunk index (finalize.cu) and round to bf16.
+// the rows of each batch entry are cut into chunks of kChunkRows = 32; in a
+// chunk every column sums its 32 rows in increasing order from zero; the
+// chunk sums combine by a stride tree over the chunk index (finalize.cu) and
+// round to bf16.
 //
-// Two passes, so that no thread needs a whole row's parameter sums:
-//  1. adaln_bwd_stats_kernel, one row per warp pair as in the forward kernel
-//     (bulk-copied z and gh, scale rows in shared memory): the row scalars
-//     mean, rstd, c1, c2 (canonical sums) into the workspace.
-//  2. adaln_bwd_cols_kernel, one 8-column vector per thread and one chunk per
-//     CTA: the thread walks the chunk's rows in stream order, forms dz and dx
-//     from the row scalars, stores them, and keeps its columns' stream sums in
-//     registers.  z and gh were just read by pass 1 and are normally still in
-//     the L2, so the DRAM traffic stays close to one pass.
-// Workspace: [rows][4] fp32 row scalars, then the [B][chunks][NQ][D] fp32
-// chunk sums.
+// One persistent kernel does all the per-row work.  A CTA (one per SM) owns
+// the chunks blockIdx.x, blockIdx.x + gridDim.x, ... and streams them through
+// a ring of shared-memory stages, kStageRows = 2 rows of every input tensor
+// (z, gh, and gz, x where present) per stage, with the chunk's scale (and
+// gate) rows in two modulation slots, filled by bulk copies (TMA engine)
+// that complete on the stage's mbarrier.  So every input byte crosses HBM
+// once and is then read from shared memory by three warp roles:
+//  - a producer warp issues the bulk copies of each stage once the column
+//    warps have released its slot (an issuing thread can block for a
+//    microsecond on a full copy queue, so no compute warp issues them);
+//  - 2 row pairs (4 warps), one row of the stage each: the row scalars mean,
+//    rstd, c1, c2 as canonical sums (P = 32) over the shared-memory row, the
+//    row split over the pair as in the forward kernel and kept in registers
+//    for both rounds, into a per-stage slot; an mbarrier tells the column
+//    warps they are there;
+//  - 8 column warps, one 8-column vector per thread: dz and dx from the row
+//    scalars, stored straight from registers, and the chunk's parameter
+//    sums in registers, written once per chunk as [B][chunks][NQ][D] fp32
+//    partials; then each warp releases the stage to the producer.
+// The partials are then reduced by the finalize kernel (launched behind this
+// one with programmatic dependent launch).  Workspace: the partials only.
 #include <map>
 #include <mutex>
 
@@ -37,329 +46,417 @@
 
 namespace afb {
 
-constexpr int kStreams = 4;
-constexpr int kRowsPerStream = 4;
-constexpr int kChunkRows = kStreams * kRowsPerStream;
+constexpr int kChunkRows = 32;
+// Rows per ring stage.  Small stages keep more of the ring in flight: a
+// slot is refilled only once both roles are done with it, and a bulk copy
+// takes about 2 us to land under load, so 4-row stages left about one stage
+// (64 KiB) per SM in flight; one-row stages cost more in per-stage
+// bookkeeping than they gain (measured: 2 rows per stage is fastest, and 4,
+// 6 or 8 stages of 2 rows time the same).
+constexpr int kStageRows = 2;
+constexpr int kStagesPerChunk = kChunkRows / kStageRows;
+// Row pairs (4 warps).  With the 8 column warps and the producer warp that
+// makes 13 warps, at most 4 per SM sub-partition, so each may hold 128
+// registers (5 warps on one sub-partition would leave 96 each).
+constexpr int kBwdPairs = 2;
+static_assert(kBwdPairs % kStageRows == 0, "pairs per stage");
+constexpr int kBwdRowGroups = kBwdPairs / kStageRows;  // pair groups, taking stages in turn
+constexpr int kBwdRowWarps = 2 * kBwdPairs;
+constexpr int kBwdColWarps = 8;                  // one 8-column vector per thread: D <= 2048
+// One more warp streams the stages in: a bulk copy can block the issuing
+// thread for a microsecond when the copy engine's queue is full, so no
+// compute warp issues them.
+constexpr int kBwdProducerWarp = kBwdRowWarps + kBwdColWarps;
+constexpr int kBwdThreads = (kBwdProducerWarp + 1) * 32;
+// Stages: a multiple of kBwdRowGroups, so that every slot serves one pair
+// group only (each group then waits on every phase of its slots in order),
+// and at most kStagesPerChunk: the modulation slot of chunk k is refilled for
+// chunk k + 2 when stage SPC(k + 2) is issued, after the column warps
+// finished stage SPC(k + 2) - ns, which for ns <= SPC lies past chunk k.
+constexpr int kBwdMaxStages = 6;
+static_assert(kBwdMaxStages <= kStagesPerChunk && kBwdMaxStages % kBwdRowGroups == 0, "stage count");
+constexpr int kBwdModSlots = 2;
+// Per row pair: one exchange buffer of 2 sums x 2 warps x 4 fp32 pairs x 32
+// lanes.  The two rounds of a row share it: in round 2 each warp writes the
+// half it read in round 1 (pair_canonical_sum2x2 called with h ^ 1), so no
+// warp overwrites data its partner has yet to read.
+constexpr size_t kBwdXchF2 = 2 * 2 * 4 * 32;
+constexpr size_t kBwdXchBytes = kBwdPairs * kBwdXchF2 * sizeof(f2_t);
 
-// ---------------------------------------------------------------------------
-// Pass 1: row scalars.
-// ---------------------------------------------------------------------------
-constexpr int kStatPairs = 8;
-constexpr int kStatWarps = 2 * kStatPairs;
-constexpr int kStatStages = 2;
-constexpr int kStatModSlots = 2;
-// Per pair: exchange buffers A (mean), B (variance) of 2 warps x 4 pairs x 32
-// lanes, and C (c1 and c2 together) of twice that.
-constexpr size_t kStatXchF2 = 4 * 2 * 4 * 32;
-
-struct AdalnStatsArgs {
-  const uint16_t* gh;     // [rows, D]
-  const uint16_t* z;      // [rows, D]
-  const uint16_t* scale;  // [B, D]
-  float4* stats;          // [rows] (mean, rstd, c1, c2)
-  int64_t rows;
-  int64_t seq;
-  int dim;
-  float eps;
-};
-
-template <int NC, bool EXACT>
-__global__ void __launch_bounds__(kStatWarps * 32, 1)
-adaln_bwd_stats_kernel(const AdalnStatsArgs a, const int use_smods) {
-  constexpr bool SPLIT = NC >= 2;
-  constexpr int NH = SPLIT ? NC / 2 : 1;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int pair = warp >> 1;
-  const int h = warp & 1;
-  const int bar_id = 1 + pair;
-  const bool leader = h == 0 && lane == 0;
-  const int D = EXACT ? NC * 256 : a.dim;
-  const uint32_t row_bytes = static_cast<uint32_t>(D) * 2u;
-  const uint32_t stage_bytes = 2u * row_bytes;  // z | gh
-  const size_t ring_all = static_cast<size_t>(kStatPairs) * kStatStages * stage_bytes;
-  uint8_t* ring = smem + static_cast<size_t>(pair) * kStatStages * stage_bytes;
-  f2_t* xch = reinterpret_cast<f2_t*>(smem + ring_all) + pair * kStatXchF2;
-  uint8_t* mods = smem + ring_all + kStatPairs * kStatXchF2 * sizeof(f2_t);
-  uint64_t* bars0 = reinterpret_cast<uint64_t*>(mods + (use_smods ? kStatModSlots * row_bytes : 0u));
-  uint64_t* bars = bars0 + pair * kStatStages;
-  uint64_t* modbar = bars0 + kStatPairs * kStatStages;
-
-  const int64_t r0 = a.rows * blockIdx.x / gridDim.x;
-  const int64_t r1 = a.rows * (blockIdx.x + 1) / gridDim.x;
-  const int64_t b_lo = r1 > r0 ? r0 / a.seq : 0;
-  const int64_t b_hi = r1 > r0 ? (r1 - 1) / a.seq : 0;
-  const bool smods = use_smods && r1 > r0 && b_hi - b_lo < kStatModSlots;
-  if (leader) {
-    for (int s = 0; s < kStatStages; ++s) mbar_init(smem_addr(&bars[s]), 1);
-    if (pair == 0) mbar_init(smem_addr(modbar), 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_wait();
-  pdl_trigger();
-  if (smods && threadIdx.x == 0) {  // the scale rows go first, ahead of every row stage
-    const int nb = static_cast<int>(b_hi - b_lo + 1);
-    mbar_arrive_expect_tx(smem_addr(modbar), static_cast<uint32_t>(nb) * row_bytes);
-    for (int k = 0; k < nb; ++k)
-      bulk_g2s(smem_addr(mods + k * row_bytes), a.scale + (b_lo + k) * D, row_bytes, smem_addr(modbar));
-  }
-  if (smods) __syncthreads();
-
-  auto row_of = [&](int64_t j) { return r0 + pair + j * kStatPairs; };
-  auto issue = [&](int64_t j) {
-    const int64_t row = row_of(j);
-    const int s = static_cast<int>(j % kStatStages);
-    uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-    const uint32_t bar = smem_addr(&bars[s]);
-    mbar_arrive_expect_tx(bar, stage_bytes);
-    bulk_g2s(smem_addr(st), a.z + row * D, row_bytes, bar);
-    bulk_g2s(smem_addr(st + row_bytes), a.gh + row * D, row_bytes, bar);
-  };
-  if (leader) {
-    for (int j = 0; j < kStatStages && row_of(j) < r1; ++j) issue(j);
-  }
-  auto col = [&](int i) { return (lane + 32 * (SPLIT ? 2 * i + h : i)) * 8; };
-  auto ok = [&](int i) { return EXACT || col(i) < D; };
-  auto div_d = [&](float x) {
-    return EXACT ? __fmul_rn(x, 1.0f / (NC * 256)) : __fdiv_rn(x, static_cast<float>(D));
-  };
-
-  bool dead = false;
-  int64_t jdead = 0;
-  if (smods && !mbar_wait(smem_addr(modbar), 0)) dead = true;
-  for (int64_t j = 0; row_of(j) < r1; ++j) {
-    const int64_t row = row_of(j);
-    const int s = static_cast<int>(j % kStatStages);
-    const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-    if (!dead && !mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / kStatStages) & 1))) {
-      dead = true;
-      jdead = j;
-    }
-    const int64_t b = row / a.seq;
-    f2_t zf[NH][4];
-    uint4 gv[NH];
-#pragma unroll
-    for (int i = 0; i < NH; ++i) {
-      const uint4 zv = ok(i) ? lds16(st + col(i) * 2) : make_uint4(0, 0, 0, 0);
-      gv[i] = ok(i) ? lds16(st + row_bytes + col(i) * 2) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) zf[i][jj] = bf2f2(word(zv, jj));
-    }
-    // dxh = gh * scale (fp32 pairs)
-    f2_t dxh[NH][4];
-#pragma unroll
-    for (int i = 0; i < NH; ++i) {
-      const uint4 scv = !ok(i) ? make_uint4(0, 0, 0, 0)
-                        : smods ? lds16(mods + static_cast<size_t>(b - b_lo) * row_bytes + col(i) * 2)
-                                : ld_keep(a.scale + b * D + col(i));
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) dxh[i][jj] = mul2_noc(bf2f2(word(gv[i], jj)), bf2f2(word(scv, jj)));
-    }
-    // Round 1: sum(z) and sum(dxh), which need nothing else.
-    float mean, c1;
-    pair_canonical_sum2x2<NH, SPLIT>([&](int n, int i, int jj) { return n == 0 ? zf[i][jj] : dxh[i][jj]; }, xch, h,
-                                     lane, bar_id, mean, c1);
-    mean = div_d(mean);
-    c1 = div_d(c1);
-    if (!SPLIT) named_bar_sync(bar_id, 64);
-    if (leader && !dead && row_of(j + kStatStages) < r1) {  // both warps have read the stage
-      fence_proxy_async_smem();
-      issue(j + kStatStages);
-    }
-    const f2_t mm = f2(mean, mean);
-#pragma unroll
-    for (int i = 0; i < NH; ++i) {
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) zf[i][jj] = ok(i) ? sub2(zf[i][jj], mm) : 0ull;  // d = z - mean
-    }
-    // Round 2: sum(d * d) and sum(dxh * d); c2 = (sum(dxh * d) * rstd) / D.
-    float var, e;
-    pair_canonical_sum2x2<NH, SPLIT>(
-        [&](int n, int i, int jj) { return mul2_noc(n == 0 ? zf[i][jj] : dxh[i][jj], zf[i][jj]); },
-        xch + 2 * 2 * 4 * 32, h, lane, bar_id, var, e);
-    const float rstd = canonical_rstd(div_d(var), a.eps);
-    const float c2 = div_d(__fmul_rn(e, rstd));
-    if (leader && !dead) a.stats[row] = make_float4(mean, rstd, c1, c2);
-  }
-  if (leader && dead) {
-    for (int64_t k = jdead; k < jdead + kStatStages && row_of(k) < r1; ++k)
-      mbar_wait(smem_addr(&bars[k % kStatStages]), static_cast<uint32_t>((k / kStatStages) & 1));
-    if (pair == 0 && smods) mbar_wait(smem_addr(modbar), 0);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Pass 2: dz, dx and the chunk sums of the parameter gradients.  Lane group w
-// (lanes 8w .. 8w+7) of a warp runs stream w of one chunk for 8 consecutive
-// 8-column vectors: its four rows are loaded at once, so a thread makes one
-// round trip.  The stream sums combine by xor shuffles in the canonical order:
-// (p0 + p2) and (p1 + p3) across lane distance 16, then their sum across 8.
-// ---------------------------------------------------------------------------
-constexpr int kColWarps = 4;
-constexpr int kColVecsPerWarp = 8;                                   // 64 columns per warp
-constexpr int kColCols = kColWarps * kColVecsPerWarp * 8;             // 256 columns per CTA
-
-struct AdalnColsArgs {
+struct AdalnBwdArgs {
   const uint16_t* gh;     // [rows, D]
   const uint16_t* gz;     // [rows, D] or null
   const uint16_t* z;      // [rows, D]
   const uint16_t* x;      // [rows, D] (HAS_X)
   const uint16_t* gate;   // [B, D] (HAS_X)
   const uint16_t* scale;  // [B, D]
-  const float4* stats;    // [rows]
   uint16_t* dz;           // [rows, D]
   uint16_t* dx;           // [rows, D] (HAS_X)
   float* part;            // [B][chunks][NQ][D]
   int64_t seq;
-  int64_t chunks;
+  int64_t chunks;         // chunks per batch entry
+  int64_t units;          // B * chunks
   int dim;
+  float eps;
 };
 
 template <bool HAS_X>
 __host__ __device__ constexpr int bwd_nq() { return HAS_X ? 3 : 2; }
-
-// grid (ceil(D / 256), chunks, B)
 template <bool HAS_X, bool HAS_GZ>
-__global__ void __launch_bounds__(kColWarps * 32, 4)
-adaln_bwd_cols_kernel(const AdalnColsArgs a) {
+__host__ __device__ constexpr int bwd_tensors() { return 2 + (HAS_GZ ? 1 : 0) + (HAS_X ? 1 : 0); }
+
+// Shared memory: ns stages of kStageRows rows of each input tensor; two
+// modulation slots (the scale row, and the gate row with HAS_X, of a chunk's
+// batch entry); the row scalars of each stage; the row pairs' exchange
+// buffers; three mbarriers per stage (data full, scalars ready, stage
+// empty).
+__host__ __device__ constexpr size_t bwd_stage_bytes(int64_t dim, int nt) {
+  return static_cast<size_t>(nt) * kStageRows * static_cast<size_t>(dim) * 2;
+}
+__host__ __device__ constexpr size_t bwd_slot_bytes(int64_t dim, bool has_x) {
+  return static_cast<size_t>(dim) * 2 * (has_x ? 2 : 1);
+}
+__host__ __device__ constexpr size_t bwd_smem(int64_t dim, int nt, bool has_x, int ns) {
+  return static_cast<size_t>(ns) * (bwd_stage_bytes(dim, nt) + kStageRows * sizeof(float4) + 3 * sizeof(uint64_t)) +
+         kBwdModSlots * bwd_slot_bytes(dim, has_x) + kBwdXchBytes;
+}
+
+// Walks a CTA's stages in order: stage j is stage i = j % SPC of the CTA's
+// chunk k = j / SPC (SPC = kStagesPerChunk), the chunk unit blockIdx.x +
+// k * gridDim.x, rows [s0, s0 + n) of batch entry b (n < kStageRows only at
+// the end of a sequence, 0 for the unused stages of a short chunk); slot
+// j % ns of the ring with phase parity (j / ns) & 1.  Incremental, so no
+// 64-bit division per stage.
+struct BwdCursor {
+  int64_t unit, b, row0;
+  int n, i, k, slot;
+  uint32_t parity;
+  __device__ void chunk_start(const AdalnBwdArgs& a) {
+    unit = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
+    b = unit / a.chunks;
+    row0 = b * a.seq + (unit - b * a.chunks) * kChunkRows;
+  }
+  __device__ void rows(const AdalnBwdArgs& a) {
+    const int64_t left = (b + 1) * a.seq - row0;
+    n = left <= 0 ? 0 : left < kStageRows ? static_cast<int>(left) : kStageRows;
+  }
+  __device__ void init(const AdalnBwdArgs& a) {
+    i = k = slot = 0;
+    parity = 0;
+    chunk_start(a);
+    rows(a);
+  }
+  __device__ void next(const AdalnBwdArgs& a, int ns) {
+    if (++slot == ns) {
+      slot = 0;
+      parity ^= 1u;
+    }
+    if (++i == kStagesPerChunk) {
+      i = 0;
+      ++k;
+      chunk_start(a);
+    } else {
+      row0 += kStageRows;
+    }
+    rows(a);
+  }
+};
+
+// EXACT: dim == 256 * NC (no masked vectors in the row pairs).  ns: stages.
+template <int NC, bool EXACT, bool HAS_X, bool HAS_GZ>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
+  constexpr int NT = bwd_tensors<HAS_X, HAS_GZ>();
   constexpr int NQ = bwd_nq<HAS_X>();
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int D = EXACT ? NC * 256 : a.dim;
+  const uint32_t tensor_bytes = static_cast<uint32_t>(kStageRows * D * 2);  // one tensor of a stage
+  const uint32_t stage_bytes = NT * tensor_bytes;
+  const uint32_t slot_bytes = static_cast<uint32_t>(bwd_slot_bytes(D, HAS_X));
+  uint8_t* mods = smem + static_cast<size_t>(ns) * stage_bytes;                    // [2][scale | gate]
+  float4* scal = reinterpret_cast<float4*>(mods + kBwdModSlots * slot_bytes);      // [ns][rows]
+  f2_t* xch_all = reinterpret_cast<f2_t*>(scal + ns * kStageRows);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xch_all + kBwdPairs * kBwdXchF2);
+  uint64_t* ready = full + ns;
+  uint64_t* empty = ready + ns;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t my_units =
+      a.units > static_cast<int64_t>(blockIdx.x) ? (a.units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t nstages = my_units * kStagesPerChunk;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&ready[s]), 2 * kStageRows);  // the warps of one pair group
+      mbar_init(smem_addr(&empty[s]), kBwdColWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
   pdl_wait();
   pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int w = lane >> 3;  // stream
-  const int64_t ch = blockIdx.y;
-  const int64_t b = blockIdx.z;
-  const int D = a.dim;
-  const int col = ((blockIdx.x * kColWarps + warp) * kColVecsPerWarp + (lane & 7)) * 8;
-  const bool cok = col < D;
-  const int64_t s0 = ch * kChunkRows;
 
-  float acc[NQ][8];
+  BwdCursor cur;
+  cur.init(a);
+  if (warp < kBwdRowWarps) {
+    // ---------------- row pairs: the row scalars -----------------------------
+    // Pair p takes row p % kStageRows of the stages j with
+    // j % kBwdRowGroups == p / kStageRows.  As the forward kernel: with
+    // NC = D/256 vectors of 8 elements per lane, warp h of the pair holds the
+    // vectors v = lane + 32 * c for c = 2i + h, and the last level of the
+    // canonical vector tree crosses the pair through shared memory
+    // (pair_canonical_sum2x2).
+    constexpr bool SPLIT = NC >= 2;
+    constexpr int NH = SPLIT ? NC / 2 : 1;
+    const int pair = warp >> 1;
+    const int h = warp & 1;
+    const int prow = pair % kStageRows;
+    const int group = pair / kStageRows;
+    const int bar_id = 2 + pair;
+    f2_t* xch = xch_all + pair * kBwdXchF2;
+    auto col = [&](int i) { return (lane + 32 * (SPLIT ? 2 * i + h : i)) * 8; };
+    auto ok = [&](int i) { return EXACT || col(i) < D; };
+    auto div_d = [&](float v) {
+      return EXACT ? __fmul_rn(v, 1.0f / (NC * 256)) : __fdiv_rn(v, static_cast<float>(D));
+    };
+    bool dead = false;
+    for (int64_t j = 0; j < nstages; ++j, cur.next(a, ns)) {
+      if (static_cast<int>(j % kBwdRowGroups) != group) continue;
+      const int s = cur.slot;
+      if (!dead && !mbar_wait(smem_addr(&full[s]), cur.parity)) dead = true;
+      if (dead) continue;  // no arrival: the column warps' bounded waits give up too
+      if (prow < cur.n) {
+        const uint8_t* zr = smem + static_cast<size_t>(s) * stage_bytes + static_cast<size_t>(prow) * D * 2;
+        const uint8_t* gr = zr + tensor_bytes;
+        const uint8_t* sc = mods + (cur.k & 1) * slot_bytes;
+        f2_t zf[NH][4], dxh[NH][4];
 #pragma unroll
-  for (int q = 0; q < NQ; ++q)
+        for (int i = 0; i < NH; ++i) {
+          const uint4 zv = ok(i) ? lds16(zr + col(i) * 2) : make_uint4(0, 0, 0, 0);
+          const uint4 gv = ok(i) ? lds16(gr + col(i) * 2) : make_uint4(0, 0, 0, 0);
+          const uint4 sv = ok(i) ? lds16(sc + col(i) * 2) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) acc[q][k] = 0.0f;
-  if (cok) {
-    uint4 zv[kRowsPerStream], gv[kRowsPerStream], gzv[kRowsPerStream], xv[kRowsPerStream];
-    float4 t[kRowsPerStream];
+          for (int jj = 0; jj < 4; ++jj) {
+            zf[i][jj] = bf2f2(word(zv, jj));
+            dxh[i][jj] = bf16x2_mul(word(gv, jj), word(sv, jj));  // gh * scale, exact
+          }
+        }
+        // Round 1: sum(z) and sum(dxh).
+        float mean, c1;
+        pair_canonical_sum2x2<NH, SPLIT>([&](int n, int i, int jj) { return n == 0 ? zf[i][jj] : dxh[i][jj]; },
+                                         xch, h, lane, bar_id, mean, c1);
+        mean = div_d(mean);
+        c1 = div_d(c1);
+        // Round 2: sum(d * d) and sum(dxh * d), d = z - mean (zero where masked).
+        const f2_t mm = f2(mean, mean);
 #pragma unroll
-    for (int r = 0; r < kRowsPerStream; ++r) {  // the stream's rows, all in flight at once
-      const int64_t s = s0 + r * kStreams + w;
-      if (s < a.seq) {
-        const int64_t o = (b * a.seq + s) * D + col;
-        zv[r] = ld_stream(a.z + o);
-        gv[r] = ld_stream(a.gh + o);
-        if (HAS_GZ) gzv[r] = ld_stream(a.gz + o);
-        if (HAS_X) xv[r] = ld_stream(a.x + o);
-        t[r] = a.stats[b * a.seq + s];  // mean, rstd, c1, c2
+        for (int i = 0; i < NH; ++i) {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) zf[i][jj] = ok(i) ? sub2(zf[i][jj], mm) : 0ull;
+        }
+        float var, e;
+        pair_canonical_sum2x2<NH, SPLIT>(
+            [&](int n, int i, int jj) { return mul2_noc(n == 0 ? zf[i][jj] : dxh[i][jj], zf[i][jj]); },
+            xch, h ^ 1, lane, bar_id, var, e);
+        const float rstd = canonical_rstd(div_d(var), a.eps);
+        const float c2 = div_d(__fmul_rn(e, rstd));
+        if (h == 0 && lane == 0) scal[s * kStageRows + prow] = make_float4(mean, rstd, c1, c2);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&ready[s]));
     }
-    float sc[8], gt[8];
-    unpack8(ld_keep(a.scale + b * D + col), sc);
-    if (HAS_X) unpack8(ld_keep(a.gate + b * D + col), gt);
+    return;
+  }
+
+  if (warp == kBwdProducerWarp) {
+    // ---------------- producer: stream the stages into the ring ------------
+    // Stage j goes into slot j % ns once the column warps have released the
+    // stage that held it before (j - ns), with the modulation rows of its
+    // chunk ahead of a chunk's first stage.
+    if (lane != 0) return;
+    bool dead = false;
+    int64_t j = 0;
+    for (; j < nstages; ++j, cur.next(a, ns)) {
+      const uint32_t bar = smem_addr(&full[cur.slot]);
+      if (j >= ns) {
+        if (!mbar_wait(smem_addr(&empty[cur.slot]), cur.parity ^ 1u)) {
+          dead = true;
+          break;
+        }
+        fence_proxy_async_smem();
+      }
+      if (cur.n == 0) {  // nothing to copy: complete the phase with a plain arrival
+        mbar_arrive(bar);
+        continue;
+      }
+      const uint32_t bytes = static_cast<uint32_t>(cur.n * D * 2);
+      const uint32_t row_bytes = static_cast<uint32_t>(D * 2);
+      const uint32_t dst = smem_addr(smem + static_cast<size_t>(cur.slot) * stage_bytes);
+      const int64_t off = cur.row0 * D;
+      const bool first = cur.i == 0;
+      mbar_arrive_expect_tx(bar, NT * bytes + (first ? (HAS_X ? 2u : 1u) * row_bytes : 0u));
+      if (first) {
+        const uint32_t slot = smem_addr(mods + (cur.k & 1) * slot_bytes);
+        bulk_g2s(slot, a.scale + cur.b * D, row_bytes, bar);
+        if (HAS_X) bulk_g2s(slot + row_bytes, a.gate + cur.b * D, row_bytes, bar);
+      }
+      bulk_g2s(dst, a.z + off, bytes, bar);
+      bulk_g2s(dst + tensor_bytes, a.gh + off, bytes, bar);
+      if (HAS_GZ) bulk_g2s(dst + 2 * tensor_bytes, a.gz + off, bytes, bar);
+      if (HAS_X) bulk_g2s(dst + (HAS_GZ ? 3 : 2) * tensor_bytes, a.x + off, bytes, bar);
+    }
+    if (dead) {  // drain the copies issued before the failed wait (bounded waits)
+      for (int64_t k = j - ns; k < j; ++k)
+        if (k >= 0) mbar_wait(smem_addr(&full[k % ns]), static_cast<uint32_t>((k / ns) & 1));
+    }
+    return;
+  }
+
+  // ---------------- column warps: dz, dx and the chunk sums ---------------
+  const int t = threadIdx.x - kBwdRowWarps * 32;
+  const int col = t * 8;
+  const bool cok = col < D;
+  bool dead = false;
+  f2_t acc[NQ][4];
+  f2_t sc[4], gt[4];
+  for (int64_t j = 0; j < nstages; ++j, cur.next(a, ns)) {
+    const int s = cur.slot;
+    if (!dead && !(mbar_wait(smem_addr(&full[s]), cur.parity) && mbar_wait(smem_addr(&ready[s]), cur.parity)))
+      dead = true;
+    if (cur.i == 0) {
 #pragma unroll
-    for (int r = 0; r < kRowsPerStream; ++r) {
-      const int64_t s = s0 + r * kStreams + w;
-      if (s >= a.seq) break;
-      const int64_t o = (b * a.seq + s) * D + col;
-      float dzf[8], dxf[8];
+      for (int q = 0; q < NQ; ++q)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float g = unpack_at(gv[r], k);
-        const float xhat = __fmul_rn(__fsub_rn(unpack_at(zv[r], k), t[r].x), t[r].y);
-        const float dxh = __fmul_rn(g, sc[k]);
-        float dz = __fmul_rn(t[r].y, __fsub_rn(__fsub_rn(dxh, t[r].z), __fmul_rn(xhat, t[r].w)));
-        if (HAS_GZ) dz = __fadd_rn(dz, unpack_at(gzv[r], k));
-        dzf[k] = dz;
-        acc[0][k] = __fadd_rn(acc[0][k], g);
-        acc[1][k] = __fadd_rn(acc[1][k], __fmul_rn(g, xhat));
+        for (int jj = 0; jj < 4; ++jj) acc[q][jj] = 0ull;
+      if (cok && !dead) {
+        const uint8_t* slot = mods + (cur.k & 1) * slot_bytes + col * 2;
+        const uint4 v = lds16(slot);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) sc[jj] = bf2f2(word(v, jj));
         if (HAS_X) {
-          dxf[k] = __fmul_rn(dz, gt[k]);
-          acc[2][k] = __fadd_rn(acc[2][k], __fmul_rn(dz, unpack_at(xv[r], k)));
+          const uint4 g = lds16(slot + D * 2);
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) gt[jj] = bf2f2(word(g, jj));
         }
       }
-      st16(a.dz + o, pack8_rn(dzf));
-      if (HAS_X) st16(a.dx + o, pack8_rn(dxf));
     }
-  }
-  // (p0 + p2) + (p1 + p3): lane groups 0/2 and 1/3 are 16 lanes apart, then
-  // groups 0/1 are 8 apart.  Commutative adds give the same bits in every lane.
+    if (cok && !dead) {
+      const uint8_t* base = smem + static_cast<size_t>(s) * stage_bytes + col * 2;
+      auto do_row = [&](int r) {
+        const uint8_t* row = base + static_cast<size_t>(r) * D * 2;
+        const uint4 zv = lds16(row);
+        const uint4 gv = lds16(row + tensor_bytes);
+        uint4 gzv = make_uint4(0, 0, 0, 0), xv = make_uint4(0, 0, 0, 0);
+        if (HAS_GZ) gzv = lds16(row + 2 * tensor_bytes);
+        if (HAS_X) xv = lds16(row + (HAS_GZ ? 3 : 2) * tensor_bytes);
+        const float4 k = scal[s * kStageRows + r];  // mean, rstd, c1, c2
+        const f2_t mm = f2(k.x, k.x), rr = f2(k.y, k.y), cc1 = f2(k.z, k.z), cc2 = f2(k.w, k.w);
+        uint4 dzo, dxo;
 #pragma unroll
-  for (int q = 0; q < NQ; ++q)
+        for (int jj = 0; jj < 4; ++jj) {
+          const f2_t g = bf2f2(word(gv, jj));
+          const f2_t xhat = mul2(sub2(bf2f2(word(zv, jj)), mm), rr);
+          const f2_t dxh = mul2_noc(g, sc[jj]);
+          const f2_t tt = sub2(sub2(dxh, cc1), mul2_noc(xhat, cc2));
+          f2_t dz;
+          if (HAS_GZ) {
+            dz = add2(mul2_noc(rr, tt), bf2f2(word(gzv, jj)));
+          } else {
+            dz = mul2(rr, tt);  // feeds multiplies only
+          }
+          word_ref(dzo, jj) = f2bf2(dz);
+          acc[0][jj] = add2(acc[0][jj], g);
+          acc[1][jj] = add2(acc[1][jj], mul2_noc(g, xhat));
+          if (HAS_X) {
+            word_ref(dxo, jj) = f2bf2(mul2(dz, gt[jj]));
+            acc[2][jj] = add2(acc[2][jj], mul2_noc(dz, bf2f2(word(xv, jj))));
+          }
+        }
+        const int64_t o = (cur.row0 + r) * D + col;
+        st16(a.dz + o, dzo);
+        if (HAS_X) st16(a.dx + o, dxo);
+      };
+      if (cur.n == kStageRows) {  // a full stage: every row, unguarded
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float v = __fadd_rn(acc[q][k], __shfl_xor_sync(kFull, acc[q][k], 16));
-      acc[q][k] = __fadd_rn(v, __shfl_xor_sync(kFull, v, 8));
+        for (int r = 0; r < kStageRows; ++r) do_row(r);
+      } else {
+        for (int r = 0; r < cur.n; ++r) do_row(r);
+      }
     }
-  if (cok && w == 0) {
-    float* out = a.part + ((b * a.chunks + ch) * NQ) * D + col;
+    // The warp is done with the stage (and, through the ready barrier, so
+    // are the row warps): release it to the producer.
+    __syncwarp();
+    if (lane == 0 && !dead) mbar_arrive(smem_addr(&empty[s]));
+    if (cur.i == kStagesPerChunk - 1 && cok && !dead) {
+      float* out = a.part + cur.unit * NQ * D + col;
 #pragma unroll
-    for (int q = 0; q < NQ; ++q) {
-      float4* o4 = reinterpret_cast<float4*>(out + q * D);
-      o4[0] = make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
-      o4[1] = make_float4(acc[q][4], acc[q][5], acc[q][6], acc[q][7]);
+      for (int q = 0; q < NQ; ++q) {
+        float4* o4 = reinterpret_cast<float4*>(out + q * D);
+        o4[0] = make_float4(f2lo(acc[q][0]), f2hi(acc[q][0]), f2lo(acc[q][1]), f2hi(acc[q][1]));
+        o4[1] = make_float4(f2lo(acc[q][2]), f2hi(acc[q][2]), f2lo(acc[q][3]), f2hi(acc[q][3]));
+      }
     }
   }
 }
 
-// Pass-1 launch plan: shared memory for the rings, exchange buffers, and (when
-// they fit) the scale slots.
-static cudaError_t launch_adaln_bwd_stats(const AdalnStatsArgs& a, cudaStream_t st) {
-  const DeviceInfo& dev = device_info();
-  if (dev.error != cudaSuccess) return dev.error;
-  const size_t row = static_cast<size_t>(a.dim) * 2;
-  const size_t base = static_cast<size_t>(kStatPairs) * kStatStages * 2 * row + kStatPairs * kStatXchF2 * sizeof(f2_t) +
-                      (kStatPairs * kStatStages + 1) * sizeof(uint64_t);
-  const int smods = base + kStatModSlots * row <= dev.max_smem_optin;
-  const size_t smem = base + (smods ? kStatModSlots * row : 0);
-  if (smem > dev.max_smem_optin) return cudaErrorInvalidValue;
-  const int nc = row_chunks(a.dim);
-  const bool exact = a.dim == 256 * nc;
-  const int64_t want = (a.rows + kStatPairs - 1) / kStatPairs;
-  const dim3 grid(static_cast<unsigned>(want < dev.sms ? want : dev.sms));
-  auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = ensure_smem(kern, smem, true);
-    if (e != cudaSuccess) return e;
-    return launch_pdl(kern, grid, dim3(kStatWarps * 32), smem, st, a, smods);
-  };
-#define AFB_LAUNCH_STATS(NC) \
-  return exact ? go(adaln_bwd_stats_kernel<NC, true>) : go(adaln_bwd_stats_kernel<NC, false>)
-  switch (nc) {
-    case 1: AFB_LAUNCH_STATS(1);
-    case 2: AFB_LAUNCH_STATS(2);
-    case 4: AFB_LAUNCH_STATS(4);
-    case 8: AFB_LAUNCH_STATS(8);
-    default: return cudaErrorInvalidValue;
-  }
-#undef AFB_LAUNCH_STATS
+// Stages that fit the shared memory (at most kBwdMaxStages).
+static int bwd_stages(int64_t dim, int nt, bool has_x, size_t limit) {
+  int n = kBwdMaxStages;
+  while (n > 0 && bwd_smem(dim, nt, has_x, n) > limit) n -= kBwdRowGroups;
+  return n;
 }
 
 template <bool HAS_X, bool HAS_GZ>
-static cudaError_t launch_adaln_bwd_cols(const AdalnColsArgs& a, int64_t batch, cudaStream_t st) {
-  const dim3 grid(static_cast<unsigned>((a.dim + kColCols - 1) / kColCols), static_cast<unsigned>(a.chunks),
-                  static_cast<unsigned>(batch));
-  // The same shared-memory carveout as the stats and finalize kernels around
-  // it, so consecutive launches need no reconfiguration of the SMs.
-  cudaError_t e = ensure_smem(adaln_bwd_cols_kernel<HAS_X, HAS_GZ>, 0, true);
-  if (e != cudaSuccess) return e;
-  return launch_pdl(adaln_bwd_cols_kernel<HAS_X, HAS_GZ>, grid, dim3(kColWarps * 32), 0, st, a);
+static cudaError_t launch_adaln_bwd(const AdalnBwdArgs& a, cudaStream_t st) {
+  const DeviceInfo& dev = device_info();
+  if (dev.error != cudaSuccess) return dev.error;
+  constexpr int NT = bwd_tensors<HAS_X, HAS_GZ>();
+  const int ns = bwd_stages(a.dim, NT, HAS_X, dev.max_smem_optin);
+  if (ns < 2 * kBwdRowGroups) return cudaErrorInvalidValue;
+  const size_t smem = bwd_smem(a.dim, NT, HAS_X, ns);
+  const int nc = row_chunks(a.dim);
+  const bool exact = a.dim == 256 * nc;
+  const dim3 grid(static_cast<unsigned>(a.units < dev.sms ? a.units : dev.sms));
+  auto go = [&](auto kern) -> cudaError_t {
+    // The same shared-memory carveout as the finalize kernel behind it.
+    cudaError_t e = ensure_smem(kern, smem, true);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(kern, grid, dim3(kBwdThreads), smem, st, a, ns);
+  };
+#define AFB_LAUNCH_BWD(NC)                                                \
+  return exact ? go(adaln_bwd_kernel<NC, true, HAS_X, HAS_GZ>) \
+               : go(adaln_bwd_kernel<NC, false, HAS_X, HAS_GZ>)
+  switch (nc) {
+    case 1: AFB_LAUNCH_BWD(1);
+    case 2: AFB_LAUNCH_BWD(2);
+    case 4: AFB_LAUNCH_BWD(4);
+    case 8: AFB_LAUNCH_BWD(8);
+    default: return cudaErrorInvalidValue;
+  }
+#undef AFB_LAUNCH_BWD
 }
 
-cudaError_t read_status_adaln_bwd(int* status) {
-  return cudaMemcpyFromSymbol(status, g_afb_device_status, sizeof(int));
-}
+cudaError_t read_status_adaln_bwd(int* status, bool clear) { return tu_status(status, clear); }
 
-static size_t adaln_bwd_stats_bytes(int64_t batch, int64_t seq) {
-  return static_cast<size_t>(batch * seq) * sizeof(float4);
+// Workspace bytes (the [B][chunks][NQ][D] fp32 partials), or false when the
+// product does not fit in size_t (absurd sizes are rejected, not wrapped).
+static bool adaln_bwd_workspace_checked(int64_t batch, int64_t seq, int64_t dim, bool has_x, size_t* out) {
+  if (batch < 0 || seq < 1 || dim < 1) {
+    *out = 0;
+    return true;
+  }
+  const unsigned __int128 chunks = static_cast<unsigned __int128>((seq + kChunkRows - 1) / kChunkRows);
+  const unsigned __int128 bytes = static_cast<unsigned __int128>(batch) * chunks * (has_x ? 3 : 2) *
+                                  static_cast<unsigned __int128>(dim) * sizeof(float);
+  if (bytes > static_cast<unsigned __int128>(SIZE_MAX)) return false;
+  *out = static_cast<size_t>(bytes);
+  return true;
 }
 
 size_t adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim, bool has_x) {
-  const int64_t chunks = (seq + kChunkRows - 1) / kChunkRows;
-  return adaln_bwd_stats_bytes(batch, seq) +
-         static_cast<size_t>(batch * chunks * (has_x ? 3 : 2) * dim) * sizeof(float);
+  size_t n = 0;
+  return adaln_bwd_workspace_checked(batch, seq, dim, has_x, &n) ? n : SIZE_MAX;
 }
 
 // Shared implementation of the two entry points (and of the workspace-free
@@ -385,35 +482,25 @@ int adaln_bwd_impl(const char* name, const void* gh, const void* gz, const void*
     return g.fail();
   if (batch == 0) return 0;
   const int64_t chunks = (seq + kChunkRows - 1) / kChunkRows;
-  float4* stats = static_cast<float4*>(workspace);
-  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + adaln_bwd_stats_bytes(batch, seq));
-  AdalnStatsArgs sa{};
-  sa.gh = static_cast<const uint16_t*>(gh);
-  sa.z = static_cast<const uint16_t*>(z);
-  sa.scale = static_cast<const uint16_t*>(scale);
-  sa.stats = stats;
-  sa.rows = batch * seq;
-  sa.seq = seq;
-  sa.dim = static_cast<int>(dim);
-  sa.eps = eps;
-  cudaError_t e = launch_adaln_bwd_stats(sa, st);
-  if (e != cudaSuccess) return g.done(e);
-  AdalnColsArgs a{};
-  a.gh = sa.gh;
+  float* part = static_cast<float*>(workspace);
+  AdalnBwdArgs a{};
+  a.gh = static_cast<const uint16_t*>(gh);
   a.gz = static_cast<const uint16_t*>(gz);
-  a.z = sa.z;
+  a.z = static_cast<const uint16_t*>(z);
   a.x = static_cast<const uint16_t*>(x);
   a.gate = static_cast<const uint16_t*>(gate);
-  a.scale = sa.scale;
-  a.stats = stats;
+  a.scale = static_cast<const uint16_t*>(scale);
   a.dz = static_cast<uint16_t*>(dz);
   a.dx = static_cast<uint16_t*>(dx);
   a.part = part;
   a.seq = seq;
   a.chunks = chunks;
+  a.units = batch * chunks;
   a.dim = static_cast<int>(dim);
-  if (has_x) e = gz ? launch_adaln_bwd_cols<true, true>(a, batch, st) : launch_adaln_bwd_cols<true, false>(a, batch, st);
-  else e = gz ? launch_adaln_bwd_cols<false, true>(a, batch, st) : launch_adaln_bwd_cols<false, false>(a, batch, st);
+  a.eps = eps;
+  cudaError_t e;
+  if (has_x) e = gz ? launch_adaln_bwd<true, true>(a, st) : launch_adaln_bwd<true, false>(a, st);
+  else e = launch_adaln_bwd<false, false>(a, st);
   if (e != cudaSuccess) return g.done(e);
   FinalizeArgs f{};
   f.part = part;
@@ -432,8 +519,8 @@ int adaln_bwd_impl(const char* name, const void* gh, const void* gz, const void*
 // cannot allocate device memory at all (a host binding with no device
 // allocator of its own, or a serving process whose device memory is fully
 // reserved at start-up and which forbids allocation on the hot path).  For
-// them the workspace (row statistics and parameter-gradient partials) lives
-// in this file-scope array instead of a caller-provided one.  Every GPU that loads the library
+// them the workspace (the parameter-gradient partials) lives in this
+// file-scope array instead of a caller-provided one.  Every GPU that loads the library
 // holds these 16 MiB until the process exits.
 // ---------------------------------------------------------------------------
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
@@ -441,7 +528,8 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / 
 
 // Device address of the scratch array for the current device.  The name of
 // the array is only a host-side stand-in; the address is looked up once per
-// device (with that device current) and cached.
+// device (with that device current) and cached, so cudaDeviceReset is not
+// supported while the library is loaded.
 static cudaError_t noalloc_scratch(void** ptr) {
   static std::mutex mu;
   static std::map<int, void*> cache;
@@ -478,10 +566,11 @@ extern "C" int afb_residual_adaln_bwd_noalloc(const void* gh, const void* gz, co
                                               void* dscale, int64_t batch, int64_t seq,
                                               int64_t dim, float eps, void* stream) {
   const char* name = "afb_residual_adaln_bwd_noalloc";
-  if (batch >= 0 && seq >= 1 && dim >= 1 &&
-      adaln_bwd_workspace(batch, seq, dim, true) > kNoAllocScratchBytes) {
+  size_t need = 0;
+  const bool fits = adaln_bwd_workspace_checked(batch, seq, dim, true, &need);
+  if (!fits || need > kNoAllocScratchBytes) {
     set_error(std::string(name) + ": this size needs " +
-              std::to_string(adaln_bwd_workspace(batch, seq, dim, true)) +
+              (fits ? std::to_string(need) : std::string("more than SIZE_MAX")) +
               " bytes of scratch, more than the " + std::to_string(kNoAllocScratchBytes) +
               " bytes this entry point holds; use afb_residual_adaln_bwd with a workspace");
     return static_cast<int>(cudaErrorInvalidValue);

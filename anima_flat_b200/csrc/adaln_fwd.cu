@@ -399,9 +399,7 @@ static cudaError_t launch_adaln(const AdalnArgs& a, cudaStream_t st) {
 #undef AFB_LAUNCH_ADALN
 }
 
-cudaError_t read_status_adaln_fwd(int* status) {
-  return cudaMemcpyFromSymbol(status, g_afb_device_status, sizeof(int));
-}
+cudaError_t read_status_adaln_fwd(int* status, bool clear) { return tu_status(status, clear); }
 
 }  // namespace afb
 

@@ -204,6 +204,15 @@ __device__ __forceinline__ float canonical_rstd(float var, float eps) {
 // own host reader (afb::read_status_* in afb_launch.h).
 static __device__ int g_afb_device_status = 0;
 constexpr int kStatusWaitTimeout = 1;
+// Host side: this translation unit's status word, then (with `clear`) zero.
+static inline cudaError_t tu_status(int* status, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_afb_device_status, sizeof(int));
+  if (e == cudaSuccess && clear && *status != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_afb_device_status, &zero, sizeof(int));
+  }
+  return e;
+}
 // try_wait suspends for a hardware-defined interval per call; this bounds a
 // wait to far beyond any real copy latency (seconds), then reports failure.
 constexpr uint32_t kMaxWaitSpins = 1u << 22;
@@ -241,9 +250,9 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 // Wait for the phase of `bar` with the given parity to complete; false (and the
-// device status set) if the bound is exhausted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kMaxWaitSpins; ++i) {
+// device status set) if the bound of `limit` try_wait rounds is exhausted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t limit = kMaxWaitSpins) {
+  for (uint32_t i = 0; i < limit; ++i) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
@@ -375,6 +384,21 @@ __device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
   return r;
 }
 __device__ __forceinline__ uint32_t word(const uint4 v, int j) {
+  return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+}
+// Exact fp32 products of the two bf16 pairs of a and b, elementwise: a bf16
+// product has at most 16 significant bits, so fma.rn.f32.bf16 with a -0
+// addend rounds exactly as the fp32 multiply of the widened operands does
+// (the sign of a zero product included), without widening them first.
+__device__ __forceinline__ f2_t bf16x2_mul(uint32_t a, uint32_t b) {
+  float lo, hi;
+  asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %2;\n mov.b32 {bl, bh}, %3;\n"
+      " fma.rn.f32.bf16 %0, al, bl, 0f80000000;\n fma.rn.f32.bf16 %1, ah, bh, 0f80000000;\n}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(a), "r"(b));
+  return f2(lo, hi);
+}
+__device__ __forceinline__ uint32_t& word_ref(uint4& v, int j) {
   return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
 }
 

@@ -38,12 +38,14 @@ cudaError_t ensure_smem(K kernel, size_t bytes, bool max_shared = false) {
 // Set by afb_set_pdl(); defaults to on unless AFB_PDL=0 is in the environment.
 bool pdl_enabled();
 
-// Host readers of the per-file device status words (OR-ed by afb_device_status).
-cudaError_t read_status_adaln_fwd(int* status);
-cudaError_t read_status_headnorm_fwd(int* status);
-cudaError_t read_status_headnorm_bwd(int* status);
-cudaError_t read_status_adaln_bwd(int* status);
-cudaError_t read_status_rms(int* status);
+// Host readers of the per-file device status words (OR-ed by
+// afb_device_status; `clear` zeroes a word after reading it).
+cudaError_t read_status_adaln_fwd(int* status, bool clear);
+cudaError_t read_status_headnorm_fwd(int* status, bool clear);
+cudaError_t read_status_headnorm_bwd(int* status, bool clear);
+cudaError_t read_status_adaln_bwd(int* status, bool clear);
+cudaError_t read_status_rms(int* status, bool clear);
+cudaError_t read_status_probe(int* status, bool clear);
 
 // Column sums of chunk partials part[batch][n][ncols] (fp32) by a stride tree
 // over the chunk index (finalize.cu); column c goes to out[c / seg][b*seg +

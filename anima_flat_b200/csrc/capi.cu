@@ -79,33 +79,31 @@ bool pdl_enabled() {
 
 extern "C" int afb_abi_version(void) { return 1; }
 
-// Device status word of the current device (0: no bounded wait ever gave up).
-extern "C" int afb_device_status(int* status) {
-  int v = 0, all = 0;
-  cudaError_t e = afb::read_status_adaln_fwd(&v);
-  all |= v;
-  if (e == cudaSuccess) {
-    e = afb::read_status_headnorm_fwd(&v);
+// Device status word of the current device (0: no bounded wait ever gave
+// up): the OR of every file's word, each cleared after reading if `clear`.
+static int device_status(int* status, bool clear, const char* name) {
+  using Reader = cudaError_t (*)(int*, bool);
+  static const Reader readers[] = {afb::read_status_adaln_fwd, afb::read_status_headnorm_fwd,
+                                   afb::read_status_headnorm_bwd, afb::read_status_adaln_bwd,
+                                   afb::read_status_rms, afb::read_status_probe};
+  int all = 0;
+  for (Reader r : readers) {
+    int v = 0;
+    const cudaError_t e = r(&v, clear);
+    if (e != cudaSuccess) {
+      afb::set_error(std::string(name) + ": " + cudaGetErrorString(e));
+      return static_cast<int>(e);
+    }
     all |= v;
-  }
-  if (e == cudaSuccess) {
-    e = afb::read_status_headnorm_bwd(&v);
-    all |= v;
-  }
-  if (e == cudaSuccess) {
-    e = afb::read_status_adaln_bwd(&v);
-    all |= v;
-  }
-  if (e == cudaSuccess) {
-    e = afb::read_status_rms(&v);
-    all |= v;
-  }
-  if (e != cudaSuccess) {
-    afb::set_error(std::string("afb_device_status: ") + cudaGetErrorString(e));
-    return static_cast<int>(e);
   }
   *status = all;
   return 0;
+}
+
+extern "C" int afb_device_status(int* status) { return device_status(status, false, "afb_device_status"); }
+
+extern "C" int afb_take_device_status(int* status) {
+  return device_status(status, true, "afb_take_device_status");
 }
 
 extern "C" const char* afb_last_error(void) { return afb::g_last_error.c_str(); }

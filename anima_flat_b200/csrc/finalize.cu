@@ -4,9 +4,8 @@
 //
 // Order: for each batch entry and column, the n chunk partials are summed by
 // a stride tree over the chunk index, zero-padded to np = pow2ceil(n):
-// p[s] += p[s + np/2], then np/4, ... down to p[0].  The tree runs in shared
-// memory: a CTA holds np partials for COLS columns and halves them level by
-// level, so the result does not depend on the launch shape.
+// p[s] += p[s + np/2], then np/4, ... down to p[0], so the result does not
+// depend on the launch shape.
 //
 // Many chunks (np > kFinalizeDirect) go through two launches computing the
 // same tree.  Its first log2(K) levels, K = np / Q, only ever combine
@@ -16,96 +15,82 @@
 // reduction; it runs first and writes the Q subtree sums over partial rows
 // [0, Q) in place (a CTA reads all of its columns before it writes them, and
 // no other CTA reads them).  The second launch is the stride tree over those
-// Q rows.  So a large reduction spreads over many CTAs instead of one CTA
-// per column block.
+// Q rows.  So a large reduction spreads over many CTAs.
 #include "afb_device.cuh"
 #include "afb_launch.h"
 
 namespace afb {
 
-constexpr int kFinalizeThreads = 256;
-constexpr int kFinalizeSmemFloats = 32768;  // 128 KiB
+constexpr int kFinalizeSmemFloats = 32768;  // largest np (finalize_fits)
 constexpr int64_t kFinalizeDirect = 1024;   // largest np reduced in one launch
 constexpr int64_t kFinalizeSplit = 256;     // Q of the two-launch form
 
-// grid: (ceil(ncols / COLS), batch); dynamic smem: np * COLS floats.  Thread t
-// owns column t % COLS of the block and the partial rows t / COLS + k * RPI, so
-// the index arithmetic is shifts and a warp's load covers whole lines.
-template <int COLS>
-__global__ void __launch_bounds__(kFinalizeThreads)
+// One CTA reduces 32 columns (lane = column) of one batch entry over np =
+// RT * NW partial rows (NW warps).  Thread (w, lane) holds the rows
+// w + NW * k, k < RT, in registers: the stride tree's levels with stride
+// np/2 .. NW pair rows of equal w, so they run in the thread (a stride tree
+// over k); the last log2(NW) levels (strides NW/2 .. 1) pair the warps' values
+// through shared memory, in warp 0.  Same order as a stride tree over all np
+// rows.  Loads of a warp cover whole 128-byte lines of a partial row.
+template <int RT>
+__global__ void __launch_bounds__(1024)
 colsum_finalize_kernel(const FinalizeArgs f) {
-  constexpr int RPI = kFinalizeThreads / COLS;  // partial rows per pass of the CTA
-  constexpr int kBatch = 8;                     // loads in flight per thread
-  extern __shared__ float sm[];
+  __shared__ float xs[32][33];
   pdl_wait();
   pdl_trigger();
-  const int t = threadIdx.x;
-  const int c = t % COLS;
-  const int r = t / COLS;
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
   const int64_t b = blockIdx.y;
-  const int col = blockIdx.x * COLS + c;
+  const int col = blockIdx.x * 32 + lane;
   const bool cok = col < f.ncols;
-  // Rows s = r, r + RPI, ..., kBatch at a time with all their loads issued
-  // before the stores into shared memory; rows past the end (and, in the
-  // strided view, floats past the batch entry's partials) read as zero.
-  const float* p = f.part + b * f.bstride;
-  const int64_t step = static_cast<int64_t>(RPI) * f.ncols;
-  int64_t at = static_cast<int64_t>(r) * f.ncols + col;  // flat index of (row s, this column)
-  for (int s0 = r; s0 < f.np; s0 += kBatch * RPI) {
-    float v[kBatch];
+  const float* p = f.part + b * f.bstride + col;
+  float v[RT];
 #pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int s = s0 + u * RPI;
-      v[u] = (cok && s < f.n && at < f.nflat) ? __ldg(p + at) : 0.0f;
-      at += step;
-    }
+  for (int k = 0; k < RT; ++k) {
+    const int64_t s = w + static_cast<int64_t>(nw) * k;
+    const int64_t at = s * f.ncols + col;  // flat index of (row s, this column)
+    v[k] = (cok && s < f.n && at < f.nflat) ? __ldg(p + s * f.ncols) : 0.0f;
+  }
 #pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int s = s0 + u * RPI;
-      if (s < f.np) sm[s * COLS + c] = v[u];
-    }
+  for (int h = RT / 2; h >= 1; h >>= 1) {
+#pragma unroll
+    for (int k = 0; k < h; ++k) v[k] = __fadd_rn(v[k], v[k + h]);
   }
-  for (int h = f.np / 2; h >= 1; h >>= 1) {
-    __syncthreads();
-    for (int s = r; s < h; s += RPI) sm[s * COLS + c] = __fadd_rn(sm[s * COLS + c], sm[(s + h) * COLS + c]);
-  }
+  xs[w][lane] = v[0];
   __syncthreads();
-  if (r == 0 && cok) {
-    const int seg = col / f.seg;
-    const int64_t o = b * f.out_bstride + col % f.seg;
-    void* dst = seg == 0 ? f.out[0] : seg == 1 ? f.out[1] : f.out[2];  // no local copy of out[]
-    if (f.bf16_out) {
-      static_cast<uint16_t*>(dst)[o] = static_cast<uint16_t>(pack2_rn(sm[c], 0.0f) & 0xffffu);
-    } else {
-      static_cast<float*>(dst)[o] = sm[c];
-    }
+  if (w != 0 || !cok) return;
+  // each lane combines its own column's warp values in place
+  for (int h = nw / 2; h >= 1; h >>= 1)
+    for (int u = 0; u < h; ++u) xs[u][lane] = __fadd_rn(xs[u][lane], xs[u + h][lane]);
+  const float t0 = xs[0][lane];
+  const int seg = col / f.seg;
+  const int64_t o = b * f.out_bstride + col % f.seg;
+  void* dst = seg == 0 ? f.out[0] : seg == 1 ? f.out[1] : f.out[2];  // no local copy of out[]
+  if (f.bf16_out) {
+    static_cast<uint16_t*>(dst)[o] = static_cast<uint16_t>(pack2_rn(t0, 0.0f) & 0xffffu);
+  } else {
+    static_cast<float*>(dst)[o] = t0;
   }
 }
 
 bool finalize_fits(int64_t n) { return n >= 1 && n <= kFinalizeSmemFloats; }
 
-// One launch: f.n rows (np = pow2ceil) of f.ncols columns per batch entry.
+// One launch: f.n rows (np = pow2ceil <= kFinalizeDirect) of f.ncols columns
+// per batch entry.  RT = np / NW rows per thread, NW <= 32 warps.
 static cudaError_t launch_finalize_one(FinalizeArgs f, int64_t batch, cudaStream_t st) {
-  const DeviceInfo& dev = device_info();
-  if (dev.error != cudaSuccess) return dev.error;
   int64_t np = 1;
   while (np < f.n) np <<= 1;
-  if (np > kFinalizeSmemFloats) return cudaErrorInvalidValue;
+  if (np > kFinalizeDirect) return cudaErrorInvalidValue;
   f.np = static_cast<int>(np);
-  // Up to 32 columns per CTA (a warp's load covers a 128-byte line of a
-  // partial row), fewer while that leaves under two CTAs per SM.
-  const int64_t fit = kFinalizeSmemFloats / np;
-  int cols = 32;
-  while (cols > 1 && cols > fit) cols >>= 1;
-  while (cols > 4 && ((f.ncols + cols - 1) / cols) * batch < 2 * static_cast<int64_t>(dev.sms)) cols >>= 1;
+  int rt = static_cast<int>(np / 8);
+  rt = rt < 1 ? 1 : rt > 32 ? 32 : rt;
+  const int nw = static_cast<int>(np / rt);
   auto go = [&](auto kern) -> cudaError_t {
-    const size_t smem = static_cast<size_t>(np) * cols * sizeof(float);
-    cudaError_t e = ensure_smem(kern, smem, true);
-    if (e != cudaSuccess) return e;
-    const dim3 grid(static_cast<unsigned>((f.ncols + cols - 1) / cols), static_cast<unsigned>(batch));
-    return launch_pdl(kern, grid, dim3(kFinalizeThreads), smem, st, f);
+    const dim3 grid(static_cast<unsigned>((f.ncols + 31) / 32), static_cast<unsigned>(batch));
+    return launch_pdl(kern, grid, dim3(nw * 32), 0, st, f);
   };
-  switch (cols) {
+  switch (rt) {
     case 32: return go(colsum_finalize_kernel<32>);
     case 16: return go(colsum_finalize_kernel<16>);
     case 8: return go(colsum_finalize_kernel<8>);

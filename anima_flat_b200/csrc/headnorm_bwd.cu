@@ -353,9 +353,7 @@ static cudaError_t finalize(const HeadNormBwdArgs& a, void* dw0, void* dw1, int 
   return launch_colsum_finalize(f, 1, st);
 }
 
-cudaError_t read_status_headnorm_bwd(int* status) {
-  return cudaMemcpyFromSymbol(status, g_afb_device_status, sizeof(int));
-}
+cudaError_t read_status_headnorm_bwd(int* status, bool clear) { return tu_status(status, clear); }
 
 }  // namespace afb
 

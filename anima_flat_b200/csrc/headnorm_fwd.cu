@@ -265,9 +265,7 @@ static cudaError_t launch_headnorm(const HeadNormArgs& a, int hd, cudaStream_t s
   }
 }
 
-cudaError_t read_status_headnorm_fwd(int* status) {
-  return cudaMemcpyFromSymbol(status, g_afb_device_status, sizeof(int));
-}
+cudaError_t read_status_headnorm_fwd(int* status, bool clear) { return tu_status(status, clear); }
 
 inline bool check_heads(int64_t batch, int64_t seq, int64_t heads, int64_t hd) {
   return check(batch >= 0, "batch must be >= 0") && check(seq >= 1, "seq must be >= 1") &&

@@ -641,9 +641,7 @@ static bool check_rms(int64_t rows, int64_t C, int shuffled, int64_t H, int64_t 
                "shuffle needs an even output grid H x W (W <= 2^30) dividing the rows");
 }
 
-cudaError_t read_status_rms(int* status) {
-  return cudaMemcpyFromSymbol(status, g_afb_device_status, sizeof(int));
-}
+cudaError_t read_status_rms(int* status, bool clear) { return tu_status(status, clear); }
 
 }  // namespace afb
 

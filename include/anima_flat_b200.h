@@ -39,6 +39,20 @@ void afb_clear_error(void);
  * bounded wait on an asynchronous copy gave up (then the kernel stopped
  * early and its outputs are incomplete).  No reference counterpart. */
 int afb_device_status(int* status);
+/* The same status, after which every status word of the device is zeroed
+ * (so a caller can report a failure once and carry on).  No reference
+ * counterpart. */
+int afb_take_device_status(int* status);
+
+/* Failure-path probe of the bounded waits; no reference counterpart.  One
+ * thread starts a 1 KiB bulk copy, then waits on an mbarrier that nothing
+ * arrives on with a limit of `spins` try_wait rounds (1..65536): the wait
+ * gives up and sets the device status word, as a kernel's wait on a copy
+ * that never lands would, and the thread then drains the copy in flight and
+ * returns.  result (device, 2 x int32): [0] = 1 if the wait gave up, [1] = 1
+ * if the copy was drained.  It faults nothing; the status word stays set
+ * until afb_take_device_status. */
+int afb_wait_probe(uint32_t spins, void* result, void* stream);
 
 /* Programmatic dependent launch on (1, default) or off (0).  Also read from
  * the environment variable AFB_PDL=0 at first use. */

@@ -66,6 +66,15 @@ def ulp_diff_ok(ours_bits: np.ndarray, ref_f32: np.ndarray, ulps: float = 2.0,
     return worst <= ulps, worst
 
 
+def bf16_ulp_distance(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    """Distance in bf16 steps between two arrays of bf16 bit patterns (the
+    patterns mapped to a monotone integer line, so -0 and +0 are 0 apart)."""
+    def line(b):
+        b = b.astype(np.int32)
+        return np.where(b & 0x8000, -(b & 0x7FFF), b)
+    return np.abs(line(a_bits) - line(b_bits))
+
+
 @pytest.fixture(scope="session")
 def cuda_dev():
     if not torch.cuda.is_available():

@@ -32,15 +32,18 @@ def test_every_declared_symbol_is_exported(name):
 
 def test_signature_table_covers_compute_entry_points():
     utility = {"afb_abi_version", "afb_last_error", "afb_clear_error", "afb_set_pdl", "afb_get_pdl",
+               "afb_take_device_status",
                "afb_device_status"}
     assert set(HEADER_FUNCS) - utility == set(_lib.SIGNATURES) | set(_lib.WORKSPACE_QUERIES)
 
 
 def test_workspace_queries():
     lib = _lib.load()
-    # [B][chunks of 16 rows][3][D] fp32
-    assert lib.afb_residual_adaln_bwd_workspace(1, 4096, 2048) == 4096 * 16 + 1 * 256 * 3 * 2048 * 4
-    assert lib.afb_adaln_bwd_workspace(2, 17, 256) == 2 * 17 * 16 + 2 * 2 * 2 * 256 * 4
+    # [B][chunks of 32 rows][3][D] fp32 (the row scalars stay in shared memory)
+    assert lib.afb_residual_adaln_bwd_workspace(1, 4096, 2048) == 1 * 128 * 3 * 2048 * 4
+    assert lib.afb_adaln_bwd_workspace(2, 17, 256) == 2 * 1 * 2 * 256 * 4
+    # sizes whose workspace does not fit in size_t report SIZE_MAX instead of wrapping
+    assert lib.afb_residual_adaln_bwd_workspace(2**62, 2**40, 2048) == 2**64 - 1
     # [chunks of 8 tokens][sections][128] fp32
     assert lib.afb_qkv_norm_rope_bwd_workspace(1, 4096, 16, 128) == 512 * 2 * 128 * 4
     assert lib.afb_head_norm_bwd_workspace(1, 4096, 16, 128) == 512 * 1 * 128 * 4

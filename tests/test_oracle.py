@@ -18,7 +18,7 @@ import torch
 
 from oracle import canonical as C
 from oracle import formulation as Fm
-from tests.conftest import from_bits, golden, to_bits, ulp_diff_ok
+from tests.conftest import bf16_ulp_distance, from_bits, golden, to_bits, ulp_diff_ok
 
 ADALN_CASES = ["residual_adaln_d2048", "adaln_d2048", "residual_adaln_d256"]
 FP8_CASES = ["residual_adaln_fp8_d2048", "adaln_fp8_d2048"]
@@ -234,14 +234,19 @@ BWD_CASES = ["residual_adaln_bwd_d2048", "residual_adaln_bwd_nogz_d256", "adaln_
 
 @pytest.mark.parametrize("name", BWD_CASES)
 def test_pin_adaln_bwd(name):
-    """Per-row grads bit-exact; bf16 parameter grads equal (the reference sums
-    its partials with torch, in another order; after bf16 rounding they agree)."""
+    """Per-row grads bit-exact.  The bf16 parameter grads agree within one bf16
+    ulp: both sides sum the same fp32 products, the reference over its program
+    partials with torch .sum (adaln.py:214-216), this build over chunks of 16
+    rows, so a sum lying next to a bf16 rounding boundary can round either way."""
     g = golden(name)
     o = C.adaln_bwd(g["gh"], g["z"], g["scale"], x=g.get("x"), gate=g.get("gate"), gz=g.get("gz"),
                     eps=float(g["eps"]), mode=C.INTERP)
-    for k in ("dz", "dx", "dgate", "dshift", "dscale"):
+    for k in ("dz", "dx"):
         if k in g:
             np.testing.assert_array_equal(o[k], g[k], err_msg=k)
+    for k in ("dgate", "dshift", "dscale"):
+        if k in g:
+            assert bf16_ulp_distance(o[k], g[k]).max() <= 1, k
 
 
 def test_pin_qkv_norm_rope_bwd():

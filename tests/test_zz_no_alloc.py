@@ -66,7 +66,13 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls(B, S, D, cuda_dev):
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(cuda_dev):
-    # 2 * 4096/16 * 3 * 4096 * 4 bytes = 24 MiB > 16 MiB
-    rc = _lib.load().afb_residual_adaln_bwd_noalloc(*([16] * 11), 2, 4096, 4096, 1e-6, None)
+    # a valid backward shape whose scratch does not fit:
+    # 16 * 4096/32 * 3 * 2048 * 4 bytes = 48 MiB > 16 MiB
+    lib = _lib.load()
+    rc = lib.afb_residual_adaln_bwd_noalloc(*([16] * 11), 16, 4096, 2048, 1e-6, None)
     assert rc == 1
-    assert "more than the" in _lib.load().afb_last_error().decode()
+    assert "more than the" in lib.afb_last_error().decode()
+    # sizes whose scratch does not even fit in size_t are rejected the same way
+    rc = lib.afb_residual_adaln_bwd_noalloc(*([16] * 11), 2**62, 2**40, 2048, 1e-6, None)
+    assert rc == 1
+    assert "more than the" in lib.afb_last_error().decode()
