@@ -264,6 +264,40 @@ def main() -> None:
             arrays["gs"] = gs
         save(name, **arrays)
 
+    # Config-scale rows: 64 rows at the model's D = 2048 (and 64 tokens of the
+    # model's 16 x 128 heads), so the pin covers more than a handful of rows.
+    # A generator of its own keeps every fixture above unchanged.
+    gen.manual_seed(20261202)
+    B, S, D = 1, 64, 2048
+    x = randn(B, S, D, outliers=0.01).to(bf)
+    res = randn(B, S, D, outliers=0.01).to(bf)
+    shift, scale, gate = mods(B, D)
+    h = torch.empty_like(res)
+    z = torch.empty_like(res)
+    A._residual_adaln_kernel.fn[(B * S,)](x, res, gate, shift, scale, h, z, S, 1e-6,
+                                          D=D, BLOCK=triton.next_power_of_2(D), HAS_X=True)
+    save("residual_adaln_d2048_r64", x=x, res=res, gate=gate, shift=shift, scale=scale, h=h, z=z,
+         eps=np.float32(1e-6))
+    q = torch.empty(B, S, D, dtype=torch.float8_e4m3fn)
+    s8 = torch.empty(B * S, 1, dtype=torch.float32)
+    z8 = torch.empty_like(res)
+    F8._residual_adaln_fp8_kernel.fn[(B * S,)](x, res, gate, shift, scale, q, s8, z8, S, 1e-6,
+                                               D=D, BLOCK=D, HAS_X=True)
+    save("residual_adaln_fp8_d2048_r64", x=x, res=res, gate=gate, shift=shift, scale=scale, q=q,
+         s=s8, z=z8, eps=np.float32(1e-6))
+    hh, ww, H, hd = 8, 8, 16, 128
+    cos, sin = rope_tables(hh, ww, hd, "cpu", (4.0, 4.0))
+    qkv = randn(1, hh * ww, 3 * H * hd).to(bf)
+    qw = 1.0 + randn(hd, std=0.02)
+    kw = 1.0 + randn(hd, std=0.02)
+    qo = torch.empty(1, hh * ww, H, hd, dtype=bf)
+    ko = torch.empty_like(qo)
+    vo = torch.empty_like(qo)
+    R._qkv_norm_rope_kernel.fn[(hh * ww, 3 * triton.cdiv(H, 2))](
+        qkv, qo, ko, vo, qw, kw, cos, sin, hh * ww, 1e-5, HEADS=H, HALF=hd // 2, HPP=2)
+    save("qkv_norm_rope_s64_h16", qkv=qkv, qw=qw, kw=kw, cos=cos, sin=sin, q=qo, k=ko, v=vo,
+         heads=np.int64(H), eps=np.float32(1e-5))
+
 
 if __name__ == "__main__":
     main()
