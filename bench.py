@@ -1,7 +1,7 @@
 """Benchmark of the fused layer-op hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg2|cfg3]
+                    [--workload cfg2|cfg3|cfg5] [--legs cfg3,cfg4,cfg5|none]
 
 A step is one pass of the hot path over one batch: the fused-op sequence of
 one Cosmos-Predict2-2B denoiser forward at 1024x1024 (config 2: B=1,
@@ -13,8 +13,17 @@ forward sequence (forward_fp8, model.py:403-473) at B=2.
 
 Every call reads its own freshly generated input buffers (the step's working
 set is several GB, far above the 126 MB L2), so no input is served from L2
-by an earlier call; between steps the same holds.  The step is captured in a
-CUDA graph and launched with programmatic dependent launch.
+by an earlier call; between steps the same holds.  Every call's outputs stay
+referenced until the graph is captured, so every call writes its own
+addresses too (no output can be overwritten while still dirty in L2).  The
+step is captured in a CUDA graph and launched with programmatic dependent
+launch.
+
+The same line carries the other configurations as sub-objects (`legs`):
+cfg3, the FP8 forward step at B=2 (forward_fp8, model.py:403-473); cfg4,
+the LoRA backward step (the backward ops of the config-2 forward in reverse
+order, B=1); cfg5: 32 sequences of 4096 tokens sharded
+over the ranks (strong scaling), running the FP8 forward step.
 
 value: algorithmic HBM bytes of all ranks' steps / max-over-ranks device
 time (CUDA events), in GB/s.  e2e: the same metric through the public API
@@ -23,7 +32,8 @@ roofline: the dominant kernel (residual_adaln): the step's 84 launches of it
 replayed alone back to back, CUDA events around the replays; the isolated
 per-launch time (events around each launch, no overlap) is reported beside it.
 cpu_baseline: the reference's unfused torch fp32 eager composition on the
-host cores (rank 0, N=1), on a bounded sample (config-1 shapes).
+host cores (rank 0, N=1), on a bounded sample of the config-2 step (the
+same shapes as our arm), with the config-1 figure beside it.
 
 Multi-GPU: one process per GPU (torchrun), each rank runs the same per-rank
 workload on its own sequences (weak scaling); no collective on the data path.
@@ -160,6 +170,7 @@ class Step:
         self.timed = "residual_adaln_fp8" if fp8 else "residual_adaln"
         self.timed_hook = None  # called around launches of self.timed when instrumenting
         self.only = None  # run only the launches of this op (roofline timing)
+        self.keep = None  # a list: every call's outputs are appended (kept referenced)
 
     def _op(self, name, fn, *a, **kw):
         if self.only is not None and name != self.only:
@@ -170,6 +181,8 @@ class Step:
         out = fn(*a, **kw)
         if hook is not None:
             hook(False)
+        if self.keep is not None:
+            self.keep.append(out)
         return out
 
     def block_mods(self, l: int, j: int):
@@ -221,17 +234,72 @@ class Step:
                *self.block_mods(L, 2))
 
 
-def capture(step: Step, only: str | None = None):
+class BwdStep:
+    """Inputs and launch order of the LoRA backward's fused-op sequence (config
+    4): the backward ops of the config-2 forward in reverse call order, 84
+    residual_adaln_bwd + 28 head_norm_bwd + 28 qkv_norm_rope_bwd + 1
+    adaln_bwd, each on its own freshly generated inputs (upstream grads
+    N(0, 1e-2), activations N(0, 1))."""
+
+    def __init__(self, shape: W.Shape, device, seed: int):
+        import anima_flat_b200 as afb
+
+        self.afb = afb
+        self.s = s = shape
+        self.calls = list(reversed(["adaln_bwd" if c == "adaln" else c + "_bwd"
+                                    for c in W.bf16_forward_calls(s)]))
+        self.bytes = W.step_bytes(self.calls, s)
+        g = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+        B, S, D, H, hd = s.batch, s.seq, s.dim, s.heads, s.head_dim
+
+        def act(*dims, std=1.0):
+            return (torch.randn(*dims, generator=g, device=device) * std).to(bf)
+
+        vec = lambda: (0.1 * torch.randn(B, D, generator=g, device=device)).to(bf)
+        side = int(round(S ** 0.5))
+        self.cos, self.sin = afb.rope_tables(side, S // side, hd, device, (4.0, 4.0))
+        self.w = 1.0 + 0.02 * torch.randn(hd, generator=g, device=device)
+        self.args = []
+        for c in self.calls:
+            if c == "residual_adaln_bwd":
+                self.args.append((act(B, S, D, std=1e-2), act(B, S, D, std=1e-2), act(B, S, D),
+                                  act(B, S, D), vec(), vec() + 1, 1e-6))
+            elif c == "adaln_bwd":
+                self.args.append((act(B, S, D, std=1e-2), act(B, S, D), vec() + 1, 1e-6))
+            elif c == "qkv_norm_rope_bwd":
+                self.args.append((act(B, S, 3 * H * hd), act(B, S, H, hd, std=1e-2),
+                                  act(B, S, H, hd, std=1e-2), act(B, S, H, hd, std=1e-2), self.w,
+                                  self.w, self.cos, self.sin, H, 1e-5))
+            else:  # head_norm_bwd
+                self.args.append((act(B, S, H * hd), act(B, S, H, hd, std=1e-2), self.w, H, 1e-5))
+        self.keep = None
+        self.only = None
+
+    def run(self):
+        ops = torch.ops.anima_flat_b200
+        with torch.no_grad():
+            for c, a in zip(self.calls, self.args):
+                if self.only is not None and c != self.only:
+                    continue
+                out = getattr(ops, c)(*a)
+                if self.keep is not None:
+                    self.keep.append(out)
+
+
+def capture(step, only: str | None = None, keep_outputs: bool = False):
     """CUDA graph of one step (its outputs live in the graph's memory pool);
-    with `only`, just that op's launches of the step."""
+    with `only`, just that op's launches of the step.  With keep_outputs,
+    every call's outputs stay referenced until the capture ends, so no call
+    reuses another's output memory inside the graph."""
     step.only = only
     try:
-        return _capture(step)
+        return _capture(step, keep_outputs)
     finally:
         step.only = None
 
 
-def _capture(step: Step):
+def _capture(step, keep_outputs: bool = False):
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
@@ -240,10 +308,37 @@ def _capture(step: Step):
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        step.run()
+    step.keep = [] if keep_outputs else None
+    try:
+        with torch.cuda.graph(g):
+            step.run()
+    finally:
+        step.keep = None  # the graph's pool keeps the memory for its replays
     torch.cuda.synchronize()
     return g
+
+
+def time_replays(g, steps: int, warmup: int, barrier, device, clocks: "ClockSampler | None" = None) -> float:
+    """ms of `steps` back-to-back replays of graph g after `warmup` replays:
+    CUDA events on the current stream between barriers and synchronizes,
+    max over ranks."""
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.start()
+        time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        g.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    return max_over_ranks(t0.elapsed_time(t1), device)
 
 
 def instrumented_capture(step: Step):
@@ -276,8 +371,67 @@ def instrumented_capture(step: Step):
 
 
 # ------------------------------------------------------------ our arm --
+LEG_DESC = {
+    "cfg3": "FP8 forward step (forward_fp8, model.py:403-473) at CFG batch 2 per rank",
+    "cfg4": "LoRA backward step at batch 1 per rank: 84 residual_adaln_bwd + 28 head_norm_bwd "
+            "+ 28 qkv_norm_rope_bwd + 1 adaln_bwd, reverse forward order",
+    "cfg5": "32 sequences x 4096 tokens (batch 16 with CFG) sharded by sequence over the ranks "
+            "(strong scaling), FP8 forward step (the config-2 op set with FP8 quantisation)",
+}
+
+
+def run_leg(name: str, args, world, rank, device, barrier) -> dict:
+    """One extra configuration: its step captured in a graph and timed like
+    the headline (K replays after W, CUDA events, max over ranks)."""
+    keep = True
+    if name == "cfg3":
+        shape = W.Shape(batch=2)
+        step = Step(shape, fp8=True, device=device, seed=2345 + rank)
+        rows, nbytes = shape.rows * world, step.bytes * world
+    elif name == "cfg4":
+        shape = W.Shape(batch=1)
+        step = BwdStep(shape, device=device, seed=3456 + rank)
+        rows, nbytes = shape.rows * world, step.bytes * world
+    else:  # cfg5: this rank's sequences of 32
+        seqs = shard_sequences(32, world, rank)
+        shape = W.Shape(batch=len(seqs))
+        # Two input sets alternate: every tensor (537 MB per activation at
+        # batch 32) is far larger than L2, and so are the outputs, which are
+        # not kept: no call can find another's data in L2.
+        step = Step(shape, fp8=True, device=device, seed=4567 + rank, distinct=False)
+        full = W.Shape(batch=32)
+        rows, nbytes = full.rows, W.step_bytes(W.fp8_forward_calls(full), full)
+        keep = False
+    steps = max(1, min(args.steps, args.leg_steps))
+    g = capture(step, keep_outputs=keep)
+    ms = time_replays(g, steps, min(args.warmup, 3), barrier, device)
+    del g
+    launches = len(step.calls) * (2 if name == "cfg4" else 1)
+    peak, _ = peak_hbm()
+    gbs = nbytes * steps / (ms * 1e-3) / 1e9
+    out = {
+        "workload": LEG_DESC[name],
+        "batch_per_rank": shape.batch,
+        "rows": rows,
+        "ops_per_step": len(step.calls),
+        "steps": steps,
+        "ms_per_step": round(ms / steps, 4),
+        "gbs": round(gbs, 1),
+        "mrows_per_s": round(rows * steps / (ms * 1e-3) / 1e6, 3),
+        "frac_of_hbm_peak": round(gbs / world / peak, 4),
+        "bytes_per_step": nbytes,
+        "scaling": "strong" if name == "cfg5" else "weak",
+        "outputs_kept": keep,
+    }
+    if name == "cfg4":
+        out["gpu_launches_per_step"] = launches
+    del step
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, world, rank, local):
-    import anima_flat_b200 as afb
+    import anima_flat_b200 as afb  # noqa: F401
     from anima_flat_b200 import _lib
 
     torch.cuda.set_device(local)
@@ -288,65 +442,51 @@ def run_ours(args, world, rank, local):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     _lib.set_pdl(not args.no_pdl)
-    if args.workload == "cfg5":
-        # config 5: 32 sequences (batch 16 with CFG) sharded over the ranks
-        seqs = shard_sequences(32, world, rank)
-        shape = W.Shape(batch=len(seqs))
-        step = Step(shape, fp8=False, device=device, seed=1234 + rank, distinct=False)
-    else:
-        shape = W.Shape(batch=2 if args.workload == "cfg3" else 1)
-        step = Step(shape, fp8=args.workload == "cfg3", device=device, seed=1234 + rank)
-    n_launch = len(step.calls)
-
-    g = capture(step)
-    for _ in range(args.warmup):
-        g.replay()
-    torch.cuda.synchronize()
 
     def barrier():
         if world > 1:
             torch.distributed.barrier(device_ids=[local])
 
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    barrier()
-    torch.cuda.synchronize()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        g.replay()
-    t1.record()
-    torch.cuda.synchronize()
-    barrier()
-    ms_local = t0.elapsed_time(t1)
-    clocks = sampler.stop()
+    if args.workload == "cfg5":
+        # config 5 alone: 32 sequences (batch 16 with CFG) sharded over the ranks
+        seqs = shard_sequences(32, world, rank)
+        shape = W.Shape(batch=len(seqs))
+        step = Step(shape, fp8=True, device=device, seed=1234 + rank, distinct=False)
+    else:
+        shape = W.Shape(batch=2 if args.workload == "cfg3" else 1)
+        step = Step(shape, fp8=args.workload == "cfg3", device=device, seed=1234 + rank)
+    n_launch = len(step.calls)
+    keep = args.workload != "cfg5"
 
-    ms = max_over_ranks(ms_local, device)
+    g = capture(step, keep_outputs=keep)
+    sampler = ClockSampler(local)
+    ms = time_replays(g, args.steps, args.warmup, barrier, device, clocks=sampler)
+    clocks = sampler.stop()
+    del g
     scaling = "strong" if args.workload == "cfg5" else "weak"
     if scaling == "strong":
-        total_bytes = W.step_bytes(step.calls, W.Shape(batch=32)) * args.steps
+        full = W.Shape(batch=32)
+        total_bytes = W.step_bytes(W.fp8_forward_calls(full), full) * args.steps
         rows_total = 32 * shape.seq * args.steps
     else:
         total_bytes = step.bytes * world * args.steps
         rows_total = shape.rows * world * args.steps
     value = total_bytes / (ms * 1e-3) / 1e9
-    del g
+    recycled = None
+    if keep:
+        # the same step with the outputs recycled by the graph's pool (every
+        # call's inputs still distinct), for comparison
+        g = capture(step, keep_outputs=False)
+        ms_r = time_replays(g, args.steps, args.warmup, barrier, device)
+        del g
+        recycled = {"ms_per_step": round(ms_r / args.steps, 4),
+                    "value": round(total_bytes / (ms_r * 1e-3) / 1e9, 1)}
 
     # --- dominant kernel: the step's launches of it alone, back to back ---
     dominant = step.timed
     n_dom = step.calls.count(dominant)
-    g2 = capture(step, only=dominant)
-    for _ in range(args.warmup):
-        g2.replay()
-    torch.cuda.synchronize()
-    t0.record()
-    for _ in range(args.steps):
-        g2.replay()
-    t1.record()
-    torch.cuda.synchronize()
-    avg_ms = t0.elapsed_time(t1) / (args.steps * n_dom)
+    g2 = capture(step, only=dominant, keep_outputs=keep)
+    avg_ms = time_replays(g2, args.steps, args.warmup, barrier, device) / (args.steps * n_dom)
     del g2
     # and each launch on its own (events around every launch, no overlap)
     g3, evs = instrumented_capture(step)
@@ -367,6 +507,14 @@ def run_ours(args, world, rank, local):
 
     # --- end to end through the public API with host buffers --------------
     e2e = run_e2e(step, shape, args, world, device, barrier)
+    del step
+    torch.cuda.empty_cache()
+
+    # --- the other configurations, in the same run -------------------------
+    legs = {}
+    if args.workload == "cfg2" and args.legs != "none":
+        for name in args.legs.split(","):
+            legs[name] = run_leg(name, args, world, rank, device, barrier)
 
     line = {
         "metric": METRIC,
@@ -387,10 +535,10 @@ def run_ours(args, world, rank, local):
                         "1024x1024, 28 blocks, 141 launches",
                 "cfg3": "cfg3: Cosmos-Predict2-2B FP8 forward fused-op sequence (forward_fp8) with "
                         f"CFG batch 2, {n_launch} launches",
-                "cfg5": "cfg5: the cfg2 op sequence over 32 sequences x 4096 tokens (batch 16 with "
-                        "CFG), sequences sharded over the GPUs",
+                "cfg5": "cfg5: the FP8 forward op sequence over 32 sequences x 4096 tokens (batch 16 "
+                        "with CFG), sequences sharded over the GPUs",
             }[args.workload],
-            "global_batch": shape.batch * world,
+            "global_batch": shape.batch * world if scaling == "weak" else 32,
             "seq_len": shape.seq,
             "rows_per_gpu": shape.rows,
             "dim": shape.dim,
@@ -398,7 +546,9 @@ def run_ours(args, world, rank, local):
             "head_dim": shape.head_dim,
             "parallelism": f"rows sharded by sequence over {world} GPU(s); no collective on the hot path",
             "l2": "inputs larger than L2: every call reads distinct buffers "
-                  f"({step.bytes / 1e9:.2f} GB of algorithmic traffic per step)",
+                  f"({total_bytes / args.steps / 1e9 / (world if scaling == 'weak' else 1):.2f} GB of "
+                  "algorithmic traffic per step per GPU)"
+                  + ("; every call's outputs kept, so every call writes distinct buffers" if keep else ""),
             "cuda_graph": True,
             "pdl": not args.no_pdl,
         },
@@ -426,6 +576,10 @@ def run_ours(args, world, rank, local):
         "clocks": clocks,
         "e2e": e2e,
     }
+    if recycled is not None:
+        line["outputs_recycled"] = recycled
+    if legs:
+        line["legs"] = legs
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
     if rank == 0:
@@ -594,10 +748,9 @@ def cpu_sequence(shape: W.Shape, seed: int = 0):
     return run, W.step_bytes(W.bf16_forward_calls(s), s)
 
 
-def cpu_baseline(budget_s: float = 12.0) -> dict:
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    shape = W.Shape(seq=256)
+def _cpu_rate(shape: W.Shape, budget_s: float, max_steps: int = 1000):
+    """Steps of the CPU composition at `shape` within about budget_s seconds
+    (at least one after a warm-up step): (steps, seconds, bytes per step)."""
     run, nbytes = cpu_sequence(shape)
     run()
     n, t0 = 0, time.perf_counter()
@@ -605,14 +758,27 @@ def cpu_baseline(budget_s: float = 12.0) -> dict:
         run()
         n += 1
         el = time.perf_counter() - t0
-        if el >= budget_s or n >= 1000:
-            break
+        if el >= budget_s or n >= max_steps:
+            return n, el, nbytes
+
+
+def cpu_baseline(budget_s: float = 12.0) -> dict:
+    """The config-2 step (the shapes our arm runs) on all host threads, for a
+    bounded number of steps, and the config-1 shapes beside it."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n, el, nbytes = _cpu_rate(W.Shape(), budget_s)
+    n1, el1, nbytes1 = _cpu_rate(W.Shape(seq=256), max(1.0, budget_s / 4))
     return {"value": round(nbytes * n / el / 1e9, 3), "unit": "GB/s", "cores": threads,
             "kind": "port",
-            "sample": (f"{n} steps of the config-2 op sequence (141 ops) on config-1 shapes "
-                       "(B=1, S=256, D=2048, 16x128 heads), torch fp32 eager composition "
-                       "(oracle/formulation.py), same byte model"),
-            "seconds": round(el, 2)}
+            "sample": (f"{n} steps of the config-2 op sequence (141 ops, B=1, S=4096, D=2048, "
+                       "16x128 heads; the same shapes and byte model as our arm), torch fp32 eager "
+                       "composition (oracle/formulation.py)"),
+            "seconds": round(el, 2),
+            "same_config": True,
+            "cfg1": {"value": round(nbytes1 * n1 / el1 / 1e9, 3), "unit": "GB/s",
+                     "sample": f"{n1} steps of the same op sequence at config-1 shapes (S=256)",
+                     "seconds": round(el1, 2)}}
 
 
 def run_reference(args, world, rank):
@@ -623,9 +789,9 @@ def run_reference(args, world, rank):
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    shape = W.Shape(seq=256)
+    shape = W.Shape()  # config 2: the shapes our arm runs
     run, nbytes = cpu_sequence(shape)
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 1)):  # a CPU step needs no more warm-up than one step
         run()
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -646,14 +812,15 @@ def run_reference(args, world, rank):
         "vs_baseline": None,
         "dtype": "fp32",
         "data": "synthetic (seeded)",
-        "config": {"workload": "cfg2 op sequence (141 ops) on a bounded CPU sample: config-1 "
-                               "shapes B=1, S=256, D=2048, 16x128 heads",
-                   "global_batch": 1, "seq_len": 256, "parallelism": "host threads"},
+        "config": {"workload": "cfg2: Cosmos-Predict2-2B forward fused-op sequence (141 ops), "
+                               "1024x1024, B=1, S=4096, D=2048, 16x128 heads, on the host cores",
+                   "global_batch": 1, "seq_len": 4096, "parallelism": "host threads"},
         "mrows_per_s": round(shape.rows * args.steps / el / 1e6, 4),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
                          "kind": "port",
-                         "sample": "torch fp32 eager composition of the reference's formulas "
-                                   "(oracle/formulation.py), config-1 shapes"},
+                         "sample": f"{args.steps} steps of the config-2 op sequence, torch fp32 "
+                                   "eager composition of the reference's formulas "
+                                   "(oracle/formulation.py), config-2 shapes"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -818,6 +985,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5"], default="cfg2")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--legs", default="cfg3,cfg4,cfg5",
+                    help="extra configurations timed in the same run: comma-separated or 'none'")
+    ap.add_argument("--leg-steps", type=int, default=20, help="at most this many timed steps per leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
