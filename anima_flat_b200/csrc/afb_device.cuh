@@ -249,6 +249,13 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
+// Prefetch `bytes` (a multiple of 16, 16-byte aligned) from global memory
+// into L2, without waiting.  It brings nothing into the SM, so it may run
+// before griddepcontrol.wait: L2 is coherent for the whole GPU, and the
+// bulk copies issued after the wait read the current data from it.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 // Wait for the phase of `bar` with the given parity to complete; false (and the
 // device status set) if the bound of `limit` try_wait rounds is exhausted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t limit = kMaxWaitSpins) {

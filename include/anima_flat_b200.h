@@ -169,15 +169,17 @@ int afb_silu_probe(void* stats, void* stream);
 /* ----------------------------------------------------------------------- */
 /* Each backward entry point takes a caller-provided device workspace of at
  * least the size its *_workspace query returns (fp32 partial sums of the
- * parameter gradients, and for the AdaLN backward 16 bytes of row statistics
- * per row); it is fully overwritten and needs no zeroing.  The
+ * parameter gradients); it is fully overwritten and needs no zeroing.  The
  * parameter gradients are summed in a fixed order, so they are reproducible
- * from run to run and across GPUs. */
+ * from run to run and across GPUs.  A workspace query returns SIZE_MAX for
+ * sizes whose workspace does not fit in size_t. */
 
 /* Replaces src/kernels/adaln.py:175-233 (_residual_adaln_bwd and the
  * anima_flat::residual_adaln_bwd op, launching _residual_adaln_bwd_kernel,
  * adaln.py:111-172).  gz may be NULL.  Outputs, in the op's order: dx, dres
- * [batch, seq, dim]; dgate, dshift, dscale [batch, dim] bf16.  dim <= 2048. */
+ * [batch, seq, dim]; dgate, dshift, dscale [batch, dim] bf16.  dim <= 2048.
+ * Workspace: batch * ceil(seq / 32) * 3 * dim * 4 bytes (chunk partials of
+ * 32 rows). */
 size_t afb_residual_adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim);
 int afb_residual_adaln_bwd(const void* gh, const void* gz, const void* z, const void* x,
                            const void* gate, const void* scale, void* dx, void* dres,
@@ -191,10 +193,12 @@ int afb_residual_adaln_bwd(const void* gh, const void* gz, const void* z, const 
  * hot path).  It has no counterpart in the reference.  Same arguments and
  * outputs, without the workspace: the partial sums live in a 16 MiB array
  * inside the library, which every GPU that loads the library holds until
- * exit.  Sizes needing more (batch * seq * 16 + batch * ceil(seq/16) * 3 *
- * dim * 4 bytes, the workspace query's value) are rejected.  The first call on a device resolves the array's address; make
- * it before any stream capture.  All calls share the array: calls that
- * overlap on the GPU race. */
+ * exit.  Sizes needing more (batch * ceil(seq / 32) * 3 * dim * 4 bytes, the
+ * workspace query's value) are rejected, overflowing sizes included.  The
+ * first call on a device resolves the array's address and caches it, so make
+ * it before any stream capture, and do not call cudaDeviceReset while the
+ * library is loaded.  All calls share the array: calls that overlap on the
+ * GPU race. */
 int afb_residual_adaln_bwd_noalloc(const void* gh, const void* gz, const void* z,
                                    const void* x, const void* gate, const void* scale,
                                    void* dx, void* dres, void* dgate, void* dshift,
