@@ -131,6 +131,25 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
     fence_mbar_init();
   }
   __syncthreads();  // barriers initialised before anyone waits on them
+  // bf16 output: while the previous kernel on the stream finishes, pull the
+  // first stage of each pair and the modulation rows into L2 (prefetch_l2).
+  // Measured: the config-2 step 5.3% faster with every output kept, an
+  // isolated launch unchanged; the FP8 instantiations lost 2 us isolated, so
+  // they do not prefetch.
+  if (!FP8 && lane == 0 && h == 0) {
+    const int64_t row = r0 + pair;
+    if (row < r1) {
+      prefetch_l2(a.res + row * D, row_bytes);
+      if (HAS_X) prefetch_l2(a.x + row * D, row_bytes);
+    }
+    if (pair == 0 && smods) {
+      for (int k = 0; k < nb; ++k) {
+        prefetch_l2(a.scale + (b_lo + k) * D, row_bytes);
+        prefetch_l2(a.shift + (b_lo + k) * D, row_bytes);
+        if (HAS_X) prefetch_l2(a.gate + (b_lo + k) * D, row_bytes);
+      }
+    }
+  }
   pdl_wait();
   pdl_trigger();
   if (smods && threadIdx.x == 0) {

