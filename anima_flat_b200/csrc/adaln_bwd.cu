@@ -194,6 +194,23 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
     fence_mbar_init();
   }
   __syncthreads();
+  // While the previous kernel on the stream finishes, pull this CTA's first
+  // stage and its chunk's modulation rows into L2 (prefetch_l2).  Measured:
+  // the config-4 backward step 5% faster, isolated launches 2 us faster.
+  if (warp == kBwdProducerWarp && lane == 0 && nstages > 0) {
+    BwdCursor c0;
+    c0.init(a);
+    const uint32_t bytes = static_cast<uint32_t>(c0.n * D * 2);
+    const int64_t off = c0.row0 * D;
+    if (bytes > 0) {
+      prefetch_l2(a.z + off, bytes);
+      prefetch_l2(a.gh + off, bytes);
+      if (HAS_GZ) prefetch_l2(a.gz + off, bytes);
+      if (HAS_X) prefetch_l2(a.x + off, bytes);
+    }
+    prefetch_l2(a.scale + c0.b * D, static_cast<uint32_t>(D * 2));
+    if (HAS_X) prefetch_l2(a.gate + c0.b * D, static_cast<uint32_t>(D * 2));
+  }
   pdl_wait();
   pdl_trigger();
 

@@ -85,6 +85,18 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
     fence_mbar_init();
   }
   __syncwarp();
+  // While the previous kernel on the stream finishes, pull this warp's first
+  // unit (section 0 of its first token and its gradient) into L2
+  // (prefetch_l2).  Measured: head_norm_bwd 17.4 -> 15.9 us in a stream,
+  // isolated unchanged.  (rowquant, whose CTAs hold one or two rows, lost
+  // 1-2 us isolated with the same prefetch and does without it.)
+  if (lane == 0) {
+    const int64_t tok = static_cast<int64_t>(blockIdx.x) * kHnbWarps + warp;
+    if (tok < a.tokens) {
+      prefetch_l2(a.src + tok * a.src_row + a.q_off, sec_bytes);
+      prefetch_l2(a.dq + tok * static_cast<int64_t>(H) * HD, sec_bytes);
+    }
+  }
   pdl_wait();
   pdl_trigger();
 
