@@ -589,6 +589,46 @@ def run_ours(args, world, rank, local):
         torch.distributed.destroy_process_group()
 
 
+def bind_numa(device) -> dict:
+    """Bind this process to the host CPUs of the GPU's NUMA node (read from
+    sysfs), so that pinned host buffers allocated afterwards are local to the
+    GPU's PCIe root.  Returns what was done."""
+    try:
+        p = torch.cuda.get_device_properties(device)
+        bdf = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        node = int(Path(f"/sys/bus/pci/devices/{bdf}/numa_node").read_text().strip())
+        if node < 0:
+            return {"numa_node": None, "bound": False, "pci": bdf}
+        cpus = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        os.sched_setaffinity(0, cpus)
+        return {"numa_node": node, "bound": True, "cpus": len(cpus), "pci": bdf}
+    except Exception as e:  # no sysfs entry (containers): run unbound
+        return {"numa_node": None, "bound": False, "why": type(e).__name__}
+
+
+def copy_rates(device, nbytes: int = 256 << 20) -> dict:
+    """This rank's host-to-device and device-to-host copy bandwidth from
+    pinned memory (GB/s, CUDA events, best of 3), measured alone."""
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    out = {}
+    for name, dst, src in (("h2d_gbs", d, h), ("d2h_gbs", h, d)):
+        best = 0.0
+        for _ in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            dst.copy_(src, non_blocking=True)
+            b.record()
+            torch.cuda.synchronize()
+            best = max(best, nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
+        out[name] = round(best, 1)
+    del h, d
+    return out
+
+
 def run_e2e(step: Step, shape: W.Shape, args, world, device, barrier) -> dict:
     """The same op sequence through the public API with host buffers: each
     call's fresh inputs are copied from pinned host memory, each output is
@@ -607,6 +647,8 @@ def run_e2e(step: Step, shape: W.Shape, args, world, device, barrier) -> dict:
     H = s.heads
     B, S, D = s.batch, s.seq, s.dim
     RING = 3
+    all_cpus = os.sched_getaffinity(0)
+    numa = bind_numa(device)  # before any pinned allocation
     pin = lambda *d: torch.empty(*d, dtype=torch.bfloat16).pin_memory()
     h_qkv, h_act = pin(B, S, 3 * D), pin(B, S, D)
     h_act.copy_(step.sub[0][0].cpu())
@@ -706,10 +748,13 @@ def run_e2e(step: Step, shape: W.Shape, args, world, device, barrier) -> dict:
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(a.elapsed_time(b), device)
+    rates = copy_rates(device)  # after the timed region, this rank's own copies alone
+    os.sched_setaffinity(0, all_cpus)  # the CPU baseline runs on every host thread
     calls = W.bf16_forward_calls(s)
     val = W.step_bytes(calls, s) * world * n / (ms * 1e-3) / 1e9
     return {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms / n, 3),
+            "numa": numa, "copy_rates_this_rank": rates,
             "path": "anima_flat_b200 public API (torch custom ops -> C ABI), pinned host buffers; "
                     f"host-to-device copies, kernels and device-to-host copies on three streams, "
                     f"ordered by events, inputs in a ring of {RING} device buffers"}
@@ -832,6 +877,47 @@ PER_OPS = ["residual_adaln", "adaln", "qkv_norm_rope", "head_norm", "residual_ad
            "adaln_fp8", "rowquant", "rowquant_gelu", "residual_adaln_bwd", "adaln_bwd",
            "qkv_norm_rope_bwd", "head_norm_bwd", "ctx_scale", "ctx_scale_bwd", "ctx_scale_rowquant",
            "rms_silu", "add_rms_silu", "shuffle_rms_silu", "rms_silu_bwd"]
+
+
+def between_gemms(fn, sets, n: int, rows: int, dim: int, device) -> float:
+    """The op's marginal time where the model runs it: every launch follows a
+    bf16 GEMM of the model's projection shape ([rows, dim] x [dim, dim],
+    src/model.py:297-337), as the GEMMs and attention surround these ops in
+    a forward pass.  Two graphs, n x [GEMM, op] and n x [GEMM], CUDA events
+    around each replay; returns (t_both - t_gemm) / n in microseconds."""
+    g = torch.Generator(device=device).manual_seed(11)
+    a = torch.randn(rows, dim, generator=g, device=device).to(torch.bfloat16)
+    w = torch.randn(dim, dim, generator=g, device=device).to(torch.bfloat16)
+    outs = [torch.empty(rows, dim, dtype=torch.bfloat16, device=device) for _ in range(2)]
+    nbuf = len(sets)
+
+    def timed(with_op: bool) -> float:
+        with torch.no_grad():
+            for i in range(3):
+                torch.matmul(a, w, out=outs[i % 2])
+                if with_op:
+                    fn(*sets[i % nbuf])
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(n):
+                    torch.matmul(a, w, out=outs[i % 2])
+                    if with_op:
+                        fn(*sets[i % nbuf])
+            graph.replay()
+            torch.cuda.synchronize()
+            best = float("inf")
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            del graph
+        return best
+
+    return (timed(True) - timed(False)) * 1e3 / n
 
 
 def run_per_op(args):
@@ -963,6 +1049,7 @@ def run_per_op(args):
             iso = sorted(x.elapsed_time(y) * 1e3 for x, y in ev)
             us_iso = iso[len(iso) // 2]
             del graph
+            between = between_gemms(fn, sets, n, B * S, D, device) if args.between_gemms else None
         shape = ({"batch": 1, "height": 1024, "width": 1024, "channels": W.VAE_C} if "rms_silu" in name
                  else {"batch": B, "seq": S, "dim": D, "heads": H, "head_dim": hd})
         print(json.dumps({
@@ -972,6 +1059,8 @@ def run_per_op(args):
             "frac_stream": round(nbytes / us_stream / 1e3 / peak, 4),
             "us_isolated_median": round(us_iso, 3), "gbs_isolated": round(nbytes / us_iso / 1e3, 1),
             "frac_isolated": round(nbytes / us_iso / 1e3 / peak, 4),
+            **({"us_between_gemms": round(between, 3),
+                "frac_between_gemms": round(nbytes / between / 1e3 / peak, 4)} if between else {}),
             "peak_gbs": peak, "peak_source": peak_src, "pdl": not args.no_pdl}), flush=True)
         del sets
         torch.cuda.empty_cache()
@@ -993,6 +1082,8 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--op", default=None,
                     help="per-op table instead of the step: 'all' or comma-separated op names")
+    ap.add_argument("--between-gemms", action="store_true",
+                    help="with --op: also time each op where every launch follows a model-shaped GEMM")
     ap.add_argument("--op-batch", type=int, default=0,
                     help="batch of the per-op shapes (default: the op's config, 1 or 2)")
     args = ap.parse_args()
