@@ -611,7 +611,9 @@ def bind_numa(device) -> dict:
 
 def copy_rates(device, nbytes: int = 256 << 20) -> dict:
     """This rank's host-to-device and device-to-host copy bandwidth from
-    pinned memory (GB/s, CUDA events, best of 3), measured alone."""
+    pinned memory (GB/s, CUDA events, best of 3), each direction on its own;
+    with several ranks, every rank copies at the same time, so the figures
+    show what each rank gets of the shared host links."""
     h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     d = torch.empty(nbytes, dtype=torch.uint8, device=device)
     out = {}
@@ -748,7 +750,7 @@ def run_e2e(step: Step, shape: W.Shape, args, world, device, barrier) -> dict:
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(a.elapsed_time(b), device)
-    rates = copy_rates(device)  # after the timed region, this rank's own copies alone
+    rates = copy_rates(device)  # after the timed region
     os.sched_setaffinity(0, all_cpus)  # the CPU baseline runs on every host thread
     calls = W.bf16_forward_calls(s)
     val = W.step_bytes(calls, s) * world * n / (ms * 1e-3) / 1e9
