@@ -373,12 +373,12 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const f2_t g = bf2f2(word(gv, jj));
-          const f2_t xhat = mul2(sub2(bf2f2(word(zv, jj)), mm), rr);
+          const f2_t xhat = mul2(bf16x2_sub_f2(word(zv, jj), mm), rr);
           const f2_t dxh = mul2_noc(g, sc[jj]);
           const f2_t tt = sub2(sub2(dxh, cc1), mul2_noc(xhat, cc2));
           f2_t dz;
           if (HAS_GZ) {
-            dz = add2(mul2_noc(rr, tt), bf2f2(word(gzv, jj)));
+            dz = bf16x2_add_f2(word(gzv, jj), mul2_noc(rr, tt));
           } else {
             dz = mul2(rr, tt);  // feeds multiplies only
           }

@@ -405,6 +405,25 @@ __device__ __forceinline__ f2_t bf16x2_mul(uint32_t a, uint32_t b) {
       : "r"(a), "r"(b));
   return f2(lo, hi);
 }
+// (lo(w) - m.lo, hi(w) - m.hi) and (lo(w) + m.lo, hi(w) + m.hi) for a bf16
+// pair w and an fp32 pair m, each one IEEE fp32 operation on the exactly
+// widened bf16 value (sub/add.rn.f32.bf16), without widening w first.
+__device__ __forceinline__ f2_t bf16x2_sub_f2(uint32_t w, f2_t m) {
+  float lo, hi;
+  asm("{\n .reg .b16 wl, wh;\n mov.b32 {wl, wh}, %2;\n"
+      " sub.rn.f32.bf16 %0, wl, %3;\n sub.rn.f32.bf16 %1, wh, %4;\n}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(w), "f"(f2lo(m)), "f"(f2hi(m)));
+  return f2(lo, hi);
+}
+__device__ __forceinline__ f2_t bf16x2_add_f2(uint32_t w, f2_t m) {
+  float lo, hi;
+  asm("{\n .reg .b16 wl, wh;\n mov.b32 {wl, wh}, %2;\n"
+      " add.rn.f32.bf16 %0, wl, %3;\n add.rn.f32.bf16 %1, wh, %4;\n}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(w), "f"(f2lo(m)), "f"(f2hi(m)));
+  return f2(lo, hi);
+}
 __device__ __forceinline__ uint32_t& word_ref(uint4& v, int j) {
   return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
 }
