@@ -124,6 +124,12 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
     bulk_g2s(smem_addr(st + sec_bytes), (sec ? a.dk : a.dq) + tok * static_cast<int64_t>(H) * HD, sec_bytes,
              bar);
   };
+  auto prefetch = [&](int64_t u) {  // lane 0: unit u's section and gradient into L2
+    const int64_t tok = token_of(u / NSEC);
+    const int sec = static_cast<int>(u % NSEC);
+    prefetch_l2(a.src + tok * a.src_row + (sec ? a.k_off : a.q_off), sec_bytes);
+    prefetch_l2((sec ? a.dk : a.dq) + tok * static_cast<int64_t>(H) * HD, sec_bytes);
+  };
   if (lane == 0) {
     for (int u = 0; u < nsw && unit_exists(u); ++u) issue(u, u);
   }
@@ -163,6 +169,11 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
           dead = true;
           break;
         }
+        // The unit that will refill this slot after it: start pulling it into
+        // L2 now, so that its bulk copy, issued once this unit is done, reads
+        // L2 instead of waiting on DRAM.  Measured: qkv_norm_rope_bwd 33.9 ->
+        // 31.9 us in a stream, 40.5 -> 38.4 us isolated; head_norm_bwd unchanged.
+        if (lane == 0 && unit_exists(u + nsw)) prefetch(u + nsw);
         const uint8_t* xin = st;
         const uint8_t* gin = st + sec_bytes;
         // The section's norm weights (L1-resident) and its weight-gradient sums.
