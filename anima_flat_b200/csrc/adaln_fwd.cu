@@ -313,7 +313,7 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
             const f2_t v = ypair(i, jj, sc, sh);
             y[i][2 * jj] = f2lo(v);
             y[i][2 * jj + 1] = f2hi(v);
-            amax = fmaxf(amax, fmaxf(fabsf(y[i][2 * jj]), fabsf(y[i][2 * jj + 1])));
+            amax = max_abs2(amax, y[i][2 * jj], y[i][2 * jj + 1]);
           }
         }
       }

@@ -115,6 +115,14 @@ __device__ __forceinline__ float round_bf(float x) {
 // to -448 as the clamp's max(NaN, -448) does.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float clamp448(float v) { return fmaxf(v, -448.0f); }
+// max(a, |b|, |c|) in one three-input max (sm_100).  Like fmaxf, it returns
+// the largest input that is not NaN.  Measured: residual_adaln_fp8 25.1 ->
+// 24.3 us against two two-input maxima.
+__device__ __forceinline__ float max_abs2(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(fabsf(b)), "f"(fabsf(c)));
+  return r;
+}
 __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   unsigned short r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));

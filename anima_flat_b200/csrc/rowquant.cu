@@ -104,7 +104,7 @@ rowquant_kernel(const RowquantArgs a) {
         f2_t v = bf2f2(word(xv[c][j >> 2], j & 3));
         if (CTX) v = bf2f2(f2bf2(mul2(v, g2)));
         y2[c][j] = GELU ? fast_gelu2(v) : v;
-        amax = fmaxf(amax, fmaxf(fabsf(f2lo(y2[c][j])), fabsf(f2hi(y2[c][j]))));
+        amax = max_abs2(amax, f2lo(y2[c][j]), f2hi(y2[c][j]));
       }
     }
   }
