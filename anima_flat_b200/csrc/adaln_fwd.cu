@@ -50,6 +50,7 @@ struct AdalnArgs {
   float* s;               // [rows] fp32 row scales (FP8 mode)
   int64_t rows;
   int64_t seq;            // rows per batch entry: b = row / seq
+  DivU32 seqd;            // division by seq
   int dim;
   float eps;
 };
@@ -166,9 +167,8 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
   if (smods) __syncthreads();
 
   auto row_of = [&](int64_t j) { return r0 + pair + j * P; };
-  auto issue = [&](int64_t j) {  // leader: stream row row_of(j) into stage j % nsw
+  auto issue = [&](int64_t j, int s) {  // leader: stream row row_of(j) into stage s = j % nsw
     const int64_t row = row_of(j);
-    const int s = static_cast<int>(j % nsw);
     uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
     mbar_arrive_expect_tx(bar, stage_bytes);
@@ -176,7 +176,7 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
     if (HAS_X) bulk_g2s(smem_addr(st + row_bytes), a.x + row * D, row_bytes, bar);
   };
   if (leader) {
-    for (int j = 0; j < nsw && row_of(j) < r1; ++j) issue(j);
+    for (int j = 0; j < nsw && row_of(j) < r1; ++j) issue(j, j);
   }
   auto col = [&](int i) { return (lane + 32 * (SPLIT ? 2 * i + h : i)) * 8; };
   auto ok = [&](int i) { return EXACT || col(i) < D; };
@@ -202,16 +202,19 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
                  : ld_keep(a.gate + b * D + c);
   };
 
+  // Stage s = j % nsw of row j and its phase parity (j / nsw) & 1, advanced
+  // with j (no division in the loop).
+  int s = 0;
+  uint32_t ph = 0;
   for (int64_t j = 0; row_of(j) < r1; ++j) {
     const int64_t row = row_of(j);
-    const int s = static_cast<int>(j % nsw);
     const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-    if (!dead && !mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
+    if (!dead && !mbar_wait(smem_addr(&bars[s]), ph)) {
       dead = true;
       jdead = j;
     }
     const bool store = writer && !dead;
-    const int64_t b = row / a.seq;
+    const int64_t b = div_u32(a.seqd, row);
     const int64_t base = row * D;
 
     // stage -> registers; z = bf16(res + bf16(gate * x)) in packed bf16x2;
@@ -229,7 +232,7 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
         named_bar_sync(bar_id, 64);
         if (leader && !dead && row_of(j + nsw) < r1) {
           fence_proxy_async_smem();
-          issue(j + nsw);
+          issue(j + nsw, s);
         }
       }
       if (HAS_X) {
@@ -264,7 +267,7 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
       if (!SPLIT) named_bar_sync(bar_id, 64);
       if (leader && !dead && row_of(j + nsw) < r1) {
         fence_proxy_async_smem();
-        issue(j + nsw);
+        issue(j + nsw, s);
       }
     }
     const f2_t mm = f2(mean, mean);
@@ -340,6 +343,10 @@ adaln_fwd_kernel(const AdalnArgs a, const int nsw, const int use_smods, const in
         if (ok(i) && store) st8(a.q + base + col(i), code[i]);
       }
       if (leader && !dead) a.s[row] = sc;
+    }
+    if (++s == nsw) {
+      s = 0;
+      ph ^= 1u;
     }
   }
   if (leader && dead) {
@@ -444,6 +451,7 @@ extern "C" int afb_residual_adaln(const void* x, const void* residual, const voi
   a.z = static_cast<uint16_t*>(z);
   a.rows = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.dim = static_cast<int>(dim);
   a.eps = eps;
   return g.done(launch_adaln<true, false>(a, static_cast<cudaStream_t>(stream)));
@@ -463,6 +471,7 @@ extern "C" int afb_adaln(const void* z, const void* shift, const void* scale, vo
   a.h = static_cast<uint16_t*>(h);
   a.rows = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.dim = static_cast<int>(dim);
   a.eps = eps;
   return g.done(launch_adaln<false, false>(a, static_cast<cudaStream_t>(stream)));
@@ -489,6 +498,7 @@ extern "C" int afb_residual_adaln_fp8(const void* x, const void* residual, const
   a.z = static_cast<uint16_t*>(z);
   a.rows = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.dim = static_cast<int>(dim);
   a.eps = eps;
   return g.done(launch_adaln<true, true>(a, static_cast<cudaStream_t>(stream)));
@@ -511,6 +521,7 @@ extern "C" int afb_adaln_fp8(const void* z, const void* shift, const void* scale
   a.s = static_cast<float*>(s);
   a.rows = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.dim = static_cast<int>(dim);
   a.eps = eps;
   return g.done(launch_adaln<false, true>(a, static_cast<cudaStream_t>(stream)));

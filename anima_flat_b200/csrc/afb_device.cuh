@@ -47,6 +47,46 @@ __device__ __forceinline__ void pdl_trigger() {
 }
 
 // ---------------------------------------------------------------------------
+// Division by a divisor fixed for a launch (the sequence length), by a
+// multiply-high and two shifts instead of a 64-bit division in the row loop.
+// The method is Granlund and Montgomery's ("Division by invariant integers
+// using multiplication", PLDI 1994, unsigned case with N = 32): for
+// 1 <= d <= 2^32 and 0 <= n < 2^32, with l = ceil(log2 d),
+//   m = floor(2^32 (2^l - d) / d) + 1   (< 2^32),
+//   t = mulhi(m, n),  q = (t + ((n - t) >> min(l, 1))) >> max(l - 1, 0).
+// Dividends of 2^32 or more, and divisors above 2^32, take the 64-bit
+// division.
+// ---------------------------------------------------------------------------
+struct DivU32 {
+  int64_t d;
+  uint32_t m;
+  uint32_t s1, s2;
+  uint32_t wide;  // d > 2^32: always the 64-bit division
+};
+__host__ inline DivU32 make_divu32(int64_t d) {
+  DivU32 v{};
+  v.d = d < 1 ? 1 : d;
+  if (v.d > (int64_t{1} << 32)) {
+    v.wide = 1;
+    return v;
+  }
+  uint32_t l = 0;
+  while ((int64_t{1} << l) < v.d) ++l;
+  const unsigned __int128 num = (static_cast<unsigned __int128>(1) << 32) *
+                                ((static_cast<unsigned __int128>(1) << l) - static_cast<uint64_t>(v.d));
+  v.m = static_cast<uint32_t>(num / static_cast<uint64_t>(v.d) + 1);
+  v.s1 = l < 1 ? l : 1;
+  v.s2 = l > 1 ? l - 1 : 0;
+  return v;
+}
+__device__ __forceinline__ int64_t div_u32(const DivU32& v, int64_t n) {
+  if (v.wide || (static_cast<uint64_t>(n) >> 32) != 0) return n / v.d;
+  const uint32_t n32 = static_cast<uint32_t>(n);
+  const uint32_t t = __umulhi(v.m, n32);
+  return static_cast<int64_t>((t + ((n32 - t) >> v.s1)) >> v.s2);
+}
+
+// ---------------------------------------------------------------------------
 // 16-byte global accesses.
 // ---------------------------------------------------------------------------
 // Streamed read-once activation: read-only path, no L1 allocation.

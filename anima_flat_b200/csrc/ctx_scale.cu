@@ -34,6 +34,7 @@ struct CtxScaleArgs {
   float* dlse;           // [B, H, S] (backward)
   int64_t tokens;
   int64_t seq;
+  DivU32 seqd;  // division by seq
   int heads;
 };
 
@@ -58,8 +59,8 @@ ctx_scale_kernel(const CtxScaleArgs a) {
   const int64_t t0 = a.tokens * blockIdx.x / gridDim.x;
   const int64_t t1 = a.tokens * (blockIdx.x + 1) / gridDim.x;
   for (int64_t tok = t0 + warp; tok < t1; tok += kCtxWarps) {
-    const int64_t b = tok / a.seq;
-    const int64_t s = tok % a.seq;
+    const int64_t b = div_u32(a.seqd, tok);
+    const int64_t s = tok - b * a.seq;
     const int64_t base = tok * static_cast<int64_t>(H) * HD;
     const float lnp = __ldg(a.ln_pad + b);
     uint4 xa[MAXIT], xb[MAXIT], ga[MAXIT], gb[MAXIT];
@@ -167,6 +168,7 @@ extern "C" int afb_ctx_scale(const void* out, const void* lse, const void* ln_pa
   a.y = static_cast<uint16_t*>(y);
   a.tokens = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.heads = static_cast<int>(heads);
   return g.done(launch_ctx_scale<false>(a, static_cast<int>(head_dim), static_cast<cudaStream_t>(stream)));
 }
@@ -188,6 +190,7 @@ extern "C" int afb_ctx_scale_bwd(const void* out, const void* lse, const void* l
   a.dlse = static_cast<float*>(dlse);
   a.tokens = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.heads = static_cast<int>(heads);
   return g.done(launch_ctx_scale<true>(a, static_cast<int>(head_dim), static_cast<cudaStream_t>(stream)));
 }

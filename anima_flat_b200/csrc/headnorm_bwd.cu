@@ -53,6 +53,7 @@ struct HeadNormBwdArgs {
   float* part;          // [chunks][NSEC][hd] chunk sums of the weight gradient
   int64_t tokens;
   int64_t seq;
+  DivU32 seqd;          // division by seq
   int heads;
   float eps;
 };
@@ -144,7 +145,7 @@ headnorm_bwd_kernel(const HeadNormBwdArgs a, const int nsw) {
     if (has) {
       float cs[8], sn[8];
       if (ROTATE) {
-        const int64_t pos = tok % a.seq;
+        const int64_t pos = tok - div_u32(a.seqd, tok) * a.seq;
         const float* cp = a.cos + pos * HALF + 8 * l;
         const float* sp = a.sin + pos * HALF + 8 * l;
         const float4 c0 = ld_keep_f4(cp), c1 = ld_keep_f4(cp + 4);
@@ -428,6 +429,7 @@ extern "C" int afb_qkv_norm_rope_bwd(const void* qkv, const void* dq, const void
   a.part = static_cast<float*>(workspace);
   a.tokens = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.heads = static_cast<int>(heads);
   a.eps = eps;
   const int hd = static_cast<int>(head_dim);
@@ -459,6 +461,7 @@ extern "C" int afb_head_norm_bwd(const void* x, const void* dy, const void* weig
   a.part = static_cast<float*>(workspace);
   a.tokens = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.heads = static_cast<int>(heads);
   a.eps = eps;
   const int hd = static_cast<int>(head_dim);

@@ -48,6 +48,7 @@ struct HeadNormArgs {
   uint16_t* out_v;       // [tokens, heads, hd] bf16 (WITH_V)
   int64_t tokens;
   int64_t seq;
+  DivU32 seqd;           // division by seq
   int heads;
   float eps;
 };
@@ -99,7 +100,7 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
       const int64_t off = sec == 0 ? a.q_off : (sec == 1 && WITH_K) ? a.k_off : a.v_off;
       prefetch_l2(a.src + tok * a.src_row + off, sec_bytes);
       if (ROTATE && sec < NSEC) {
-        const int64_t pos = tok % a.seq;
+        const int64_t pos = tok - div_u32(a.seqd, tok) * a.seq;
         prefetch_l2(a.cos + pos * HALF, HALF * 4u);
         prefetch_l2(a.sin + pos * HALF, HALF * 4u);
       }
@@ -123,11 +124,10 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
   auto unit_of = [&](int64_t j) {
     return static_cast<int64_t>(warp) * gridDim.x + blockIdx.x + j * static_cast<int64_t>(gridDim.x) * kHeadWarps;
   };
-  auto issue = [&](int64_t j) {  // lane 0: stream unit unit_of(j) into stage j % nsw
+  auto issue = [&](int64_t j, int s) {  // lane 0: stream unit unit_of(j) into stage s = j % nsw
     const int64_t u = unit_of(j);
     const int64_t tok = u / NU;
     const int sec = static_cast<int>(u % NU);
-    const int s = static_cast<int>(j % nsw);
     uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
     const bool tab = ROTATE && sec < NSEC;
@@ -135,13 +135,13 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
     mbar_arrive_expect_tx(bar, sec_bytes + (tab ? kTabBytes : 0u));
     bulk_g2s(smem_addr(st), a.src + tok * a.src_row + off, sec_bytes, bar);
     if (tab) {
-      const int64_t pos = tok % a.seq;
+      const int64_t pos = tok - div_u32(a.seqd, tok) * a.seq;
       bulk_g2s(smem_addr(st + sec_bytes), a.cos + pos * HALF, HALF * 4u, bar);
       bulk_g2s(smem_addr(st + sec_bytes + HALF * 4u), a.sin + pos * HALF, HALF * 4u, bar);
     }
   };
   if (lane == 0) {
-    for (int j = 0; j < nsw && unit_of(j) < u1; ++j) issue(j);
+    for (int j = 0; j < nsw && unit_of(j) < u1; ++j) issue(j, j);
   }
   if (!mbar_wait(smem_addr(wbar), 0)) {
     // Never expected: drain this warp's copies (bounded), then stop.
@@ -151,13 +151,16 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
     return;
   }
 
+  // Stage s = j % nsw of unit j and its phase parity (j / nsw) & 1, advanced
+  // with j (no division in the loop).
+  int s = 0;
+  uint32_t ph = 0;
   for (int64_t j = 0; unit_of(j) < u1; ++j) {
     const int64_t u = unit_of(j);
     const int64_t tok = u / NU;
     const int sec = static_cast<int>(u % NU);
-    const int s = static_cast<int>(j % nsw);
     const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-    if (!mbar_wait(smem_addr(&bars[s]), static_cast<uint32_t>((j / nsw) & 1))) {
+    if (!mbar_wait(smem_addr(&bars[s]), ph)) {
       for (int64_t k = j + 1; k < j + nsw && unit_of(k) < u1; ++k)
         mbar_wait(smem_addr(&bars[k % nsw]), static_cast<uint32_t>((k / nsw) & 1));
       return;
@@ -253,7 +256,11 @@ headnorm_fwd_kernel(const HeadNormArgs a, const int nsw) {
     __syncwarp();
     if (lane == 0 && unit_of(j + nsw) < u1) {
       fence_proxy_async_smem();
-      issue(j + nsw);
+      issue(j + nsw, s);
+    }
+    if (++s == nsw) {
+      s = 0;
+      ph ^= 1u;
     }
   }
 }
@@ -328,6 +335,7 @@ extern "C" int afb_qkv_norm_rope(const void* qkv, const void* q_weight, const vo
   a.out_v = static_cast<uint16_t*>(v);
   a.tokens = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.heads = static_cast<int>(heads);
   a.eps = eps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -351,6 +359,7 @@ extern "C" int afb_head_norm(const void* x, const void* weight, void* y, int64_t
   a.out_q = static_cast<uint16_t*>(y);
   a.tokens = batch * seq;
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.heads = static_cast<int>(heads);
   a.eps = eps;
   return g.done(launch_headnorm<false, false, false>(a, static_cast<int>(head_dim),

@@ -50,6 +50,7 @@ struct RowquantArgs {
   const float* lse;     // [B, H, S]
   const float* ln_pad;  // [B]
   int64_t seq;
+  DivU32 seqd;          // division by seq
   int heads;
   int hd_shift;         // log2(hd)
 };
@@ -83,7 +84,7 @@ rowquant_kernel(const RowquantArgs a) {
     float lse[CPL], lnp = 0.0f;
     int64_t bb = 0, ss = 0;
     if (CTX && row_ok) {
-      bb = row / a.seq;
+      bb = div_u32(a.seqd, row);
       ss = row - bb * a.seq;
       lnp = __ldg(a.ln_pad + bb);
     }
@@ -282,6 +283,7 @@ extern "C" int afb_ctx_scale_rowquant(const void* out, const void* lse, const vo
   a.lse = static_cast<const float*>(lse);
   a.ln_pad = static_cast<const float*>(ln_pad);
   a.seq = seq;
+  a.seqd = make_divu32(seq);
   a.heads = static_cast<int>(heads);
   a.hd_shift = head_dim == 64 ? 6 : head_dim == 128 ? 7 : 8;
   return g.done(launch_rowquant<false, true>(a, static_cast<cudaStream_t>(stream)));
