@@ -27,12 +27,13 @@
 //  - a producer warp issues the bulk copies of each stage once the column
 //    warps have released its slot (an issuing thread can block for a
 //    microsecond on a full copy queue, so no compute warp issues them);
-//  - 2 row pairs (4 warps), one row of the stage each: the row scalars mean,
+//  - 4 row pairs (8 warps) in two groups taking alternate stages, one row
+//    of the stage per pair: the row scalars mean,
 //    rstd, c1, c2 as canonical sums (P = 32) over the shared-memory row, the
 //    row split over the pair as in the forward kernel and kept in registers
 //    for both rounds, into a per-stage slot; an mbarrier tells the column
 //    warps they are there;
-//  - 8 column warps, one 8-column vector per thread: dz and dx from the row
+//  - 4 column warps, two 8-column vectors per thread: dz and dx from the row
 //    scalars, stored straight from registers, and the chunk's parameter
 //    sums in registers, written once per chunk as [B][chunks][NQ][D] fp32
 //    partials; then each warp releases the stage to the producer.
@@ -55,14 +56,20 @@ constexpr int kChunkRows = 32;
 // 6 or 8 stages of 2 rows time the same).
 constexpr int kStageRows = 2;
 constexpr int kStagesPerChunk = kChunkRows / kStageRows;
-// Row pairs (4 warps).  With the 8 column warps and the producer warp that
-// makes 13 warps, at most 4 per SM sub-partition, so each may hold 128
-// registers (5 warps on one sub-partition would leave 96 each).
-constexpr int kBwdPairs = 2;
+// Row pairs (8 warps), two groups of two taking the stages in turn.  With the
+// 4 column warps and the producer warp that makes 13 warps, at most 4 per SM
+// sub-partition, so each may hold 128 registers (5 warps on one sub-partition
+// would leave 96 each).  The row scalars are the critical path (a pair's
+// row takes about a microsecond of dependent sums), so the warps go to row
+// pairs rather than column warps: measured with 2 pairs and 8 column warps
+// of one vector each, adaln_bwd 23.2 us against 21.7, residual_adaln_bwd
+// 27.3 against 27.0.
+constexpr int kBwdPairs = 4;
 static_assert(kBwdPairs % kStageRows == 0, "pairs per stage");
 constexpr int kBwdRowGroups = kBwdPairs / kStageRows;  // pair groups, taking stages in turn
 constexpr int kBwdRowWarps = 2 * kBwdPairs;
-constexpr int kBwdColWarps = 8;                  // one 8-column vector per thread: D <= 2048
+constexpr int kBwdColWarps = 4;
+constexpr int kColVecs = 2;  // 8-column vectors per column thread: D <= 2048
 // One more warp streams the stages in: a bulk copy can block the issuing
 // thread for a microsecond when the copy engine's queue is full, so no
 // compute warp issues them.
@@ -332,67 +339,93 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
 
   // ---------------- column warps: dz, dx and the chunk sums ---------------
   const int t = threadIdx.x - kBwdRowWarps * 32;
-  const int col = t * 8;
-  const bool cok = col < D;
+  auto colv = [&](int v) { return (t + v * kBwdColWarps * 32) * 8; };
   bool dead = false;
-  f2_t acc[NQ][4];
-  f2_t sc[4], gt[4];
+  f2_t acc[kColVecs][NQ][4];
+  // The modulation rows: held in registers for a chunk, or (HAS_X, where
+  // the registers are short) re-read from the shared-memory slot per row.
+  constexpr bool kModRegs = !HAS_X;
+  f2_t sc[kColVecs][4], gt[kColVecs][4];
   for (int64_t j = 0; j < nstages; ++j, cur.next(a, ns)) {
     const int s = cur.slot;
     if (!dead && !(mbar_wait(smem_addr(&full[s]), cur.parity) && mbar_wait(smem_addr(&ready[s]), cur.parity)))
       dead = true;
     if (cur.i == 0) {
 #pragma unroll
-      for (int q = 0; q < NQ; ++q)
+      for (int v = 0; v < kColVecs; ++v) {
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) acc[q][jj] = 0ull;
-      if (cok && !dead) {
-        const uint8_t* slot = mods + (cur.k & 1) * slot_bytes + col * 2;
-        const uint4 v = lds16(slot);
+        for (int q = 0; q < NQ; ++q)
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) sc[jj] = bf2f2(word(v, jj));
-        if (HAS_X) {
-          const uint4 g = lds16(slot + D * 2);
+          for (int jj = 0; jj < 4; ++jj) acc[v][q][jj] = 0ull;
+        if (kModRegs && colv(v) < D && !dead) {
+          const uint8_t* slot = mods + (cur.k & 1) * slot_bytes + colv(v) * 2;
+          const uint4 w = lds16(slot);
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) gt[jj] = bf2f2(word(g, jj));
+          for (int jj = 0; jj < 4; ++jj) sc[v][jj] = bf2f2(word(w, jj));
+          if (HAS_X) {
+            const uint4 g = lds16(slot + D * 2);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) gt[v][jj] = bf2f2(word(g, jj));
+          }
         }
       }
     }
-    if (cok && !dead) {
-      const uint8_t* base = smem + static_cast<size_t>(s) * stage_bytes + col * 2;
+    if (!dead) {
       auto do_row = [&](int r) {
-        const uint8_t* row = base + static_cast<size_t>(r) * D * 2;
-        const uint4 zv = lds16(row);
-        const uint4 gv = lds16(row + tensor_bytes);
-        uint4 gzv = make_uint4(0, 0, 0, 0), xv = make_uint4(0, 0, 0, 0);
-        if (HAS_GZ) gzv = lds16(row + 2 * tensor_bytes);
-        if (HAS_X) xv = lds16(row + (HAS_GZ ? 3 : 2) * tensor_bytes);
         const float4 k = scal[s * kStageRows + r];  // mean, rstd, c1, c2
         const f2_t mm = f2(k.x, k.x), rr = f2(k.y, k.y), cc1 = f2(k.z, k.z), cc2 = f2(k.w, k.w);
-        uint4 dzo, dxo;
+        const uint8_t* row = smem + static_cast<size_t>(s) * stage_bytes + static_cast<size_t>(r) * D * 2;
+        const int64_t o0 = (cur.row0 + r) * D;
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const f2_t g = bf2f2(word(gv, jj));
-          const f2_t xhat = mul2(bf16x2_sub_f2(word(zv, jj), mm), rr);
-          const f2_t dxh = mul2_noc(g, sc[jj]);
-          const f2_t tt = sub2(sub2(dxh, cc1), mul2_noc(xhat, cc2));
-          f2_t dz;
-          if (HAS_GZ) {
-            dz = bf16x2_add_f2(word(gzv, jj), mul2_noc(rr, tt));
+        for (int v = 0; v < kColVecs; ++v) {
+          const int col = colv(v);
+          if (col >= D) continue;
+          const uint4 zv = lds16(row + col * 2);
+          const uint4 gv = lds16(row + tensor_bytes + col * 2);
+          uint4 gzv = make_uint4(0, 0, 0, 0), xv = make_uint4(0, 0, 0, 0);
+          if (HAS_GZ) gzv = lds16(row + 2 * tensor_bytes + col * 2);
+          if (HAS_X) xv = lds16(row + (HAS_GZ ? 3 : 2) * tensor_bytes + col * 2);
+          f2_t scv[4], gtv[4];
+          if (kModRegs) {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              scv[jj] = sc[v][jj];
+              gtv[jj] = gt[v][jj];
+            }
           } else {
-            dz = mul2(rr, tt);  // feeds multiplies only
+            const uint8_t* slot = mods + (cur.k & 1) * slot_bytes + col * 2;
+            const uint4 w = lds16(slot);
+            const uint4 g = HAS_X ? lds16(slot + D * 2) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              scv[jj] = bf2f2(word(w, jj));
+              gtv[jj] = bf2f2(word(g, jj));
+            }
           }
-          word_ref(dzo, jj) = f2bf2(dz);
-          acc[0][jj] = add2(acc[0][jj], g);
-          acc[1][jj] = add2(acc[1][jj], mul2_noc(g, xhat));
-          if (HAS_X) {
-            word_ref(dxo, jj) = f2bf2(mul2(dz, gt[jj]));
-            acc[2][jj] = add2(acc[2][jj], mul2_noc(dz, bf2f2(word(xv, jj))));
+          uint4 dzo, dxo;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const f2_t g = bf2f2(word(gv, jj));
+            const f2_t xhat = mul2(bf16x2_sub_f2(word(zv, jj), mm), rr);
+            const f2_t dxh = mul2_noc(g, scv[jj]);
+            const f2_t tt = sub2(sub2(dxh, cc1), mul2_noc(xhat, cc2));
+            f2_t dz;
+            if (HAS_GZ) {
+              dz = bf16x2_add_f2(word(gzv, jj), mul2_noc(rr, tt));
+            } else {
+              dz = mul2(rr, tt);  // feeds multiplies only
+            }
+            word_ref(dzo, jj) = f2bf2(dz);
+            acc[v][0][jj] = add2(acc[v][0][jj], g);
+            acc[v][1][jj] = add2(acc[v][1][jj], mul2_noc(g, xhat));
+            if (HAS_X) {
+              word_ref(dxo, jj) = f2bf2(mul2(dz, gtv[jj]));
+              acc[v][2][jj] = add2(acc[v][2][jj], mul2_noc(dz, bf2f2(word(xv, jj))));
+            }
           }
+          st16(a.dz + o0 + col, dzo);
+          if (HAS_X) st16(a.dx + o0 + col, dxo);
         }
-        const int64_t o = (cur.row0 + r) * D + col;
-        st16(a.dz + o, dzo);
-        if (HAS_X) st16(a.dx + o, dxo);
       };
       if (cur.n == kStageRows) {  // a full stage: every row, unguarded
 #pragma unroll
@@ -405,13 +438,17 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
     // are the row warps): release it to the producer.
     __syncwarp();
     if (lane == 0 && !dead) mbar_arrive(smem_addr(&empty[s]));
-    if (cur.i == kStagesPerChunk - 1 && cok && !dead) {
-      float* out = a.part + cur.unit * NQ * D + col;
+    if (cur.i == kStagesPerChunk - 1 && !dead) {
 #pragma unroll
-      for (int q = 0; q < NQ; ++q) {
-        float4* o4 = reinterpret_cast<float4*>(out + q * D);
-        o4[0] = make_float4(f2lo(acc[q][0]), f2hi(acc[q][0]), f2lo(acc[q][1]), f2hi(acc[q][1]));
-        o4[1] = make_float4(f2lo(acc[q][2]), f2hi(acc[q][2]), f2lo(acc[q][3]), f2hi(acc[q][3]));
+      for (int v = 0; v < kColVecs; ++v) {
+        if (colv(v) >= D) continue;
+        float* out = a.part + cur.unit * NQ * D + colv(v);
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          float4* o4 = reinterpret_cast<float4*>(out + q * D);
+          o4[0] = make_float4(f2lo(acc[v][q][0]), f2hi(acc[v][q][0]), f2lo(acc[v][q][1]), f2hi(acc[v][q][1]));
+          o4[1] = make_float4(f2lo(acc[v][q][2]), f2hi(acc[v][q][2]), f2lo(acc[v][q][3]), f2hi(acc[v][q][3]));
+        }
       }
     }
   }
