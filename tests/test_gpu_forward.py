@@ -95,6 +95,43 @@ def test_adaln_fp8_bit_exact(B, S, D, has_x, cuda_dev):
     np.testing.assert_array_equal(to_bits(q), o["q"])
 
 
+@pytest.mark.parametrize("D", [2048, 1024])
+@pytest.mark.parametrize("has_x", [True, False])
+def test_adaln_fp8_nonfinite_rows(D, has_x, cuda_dev):
+    """Rows holding a NaN or an infinity (in the residual stream, or through an
+    infinite shift) take the NaN-ignoring row max and the NaN clamp to -448,
+    bit-exact against the oracle; finite rows of the same launch are
+    unaffected."""
+    B, S = 2, 7
+    r = rng(D + 7 * has_x)
+    x, res = act(r, (B, S, D)), act(r, (B, S, D))
+    shift, scale, gate = mods(r, B, D)
+    resf = from_bits(res, "cpu").float().numpy()
+    resf[0, 1, 5] = np.nan
+    resf[0, 3, 9] = np.inf
+    resf[1, 2, 17] = -np.inf
+    res = bf_bits(resf)
+    shf = from_bits(shift, "cpu").float().numpy()
+    shf[1, 33] = -np.inf
+    shift = bf_bits(shf)
+    if has_x:
+        q, s, z = afb.residual_adaln_fp8(*(dev(a, cuda_dev) for a in (x, res, gate, shift, scale)))
+        o = C.adaln_fwd(res, shift, scale, x=x, gate=gate, fp8=True)
+        # z: NaN where the oracle has NaN (the GPU writes the canonical NaN
+        # 0x7FFF, the host's arithmetic may set the sign bit), equal bits elsewhere
+        zb = to_bits(z)
+        nan = (zb & 0x7FFF) > 0x7F80
+        np.testing.assert_array_equal(nan, (o["z"] & 0x7FFF) > 0x7F80)
+        assert nan.any()
+        np.testing.assert_array_equal(zb[~nan], o["z"][~nan])
+    else:
+        q, s = afb.adaln_fp8(*(dev(a, cuda_dev) for a in (res, shift, scale)))
+        o = C.adaln_fwd(res, shift, scale, fp8=True)
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), o["s"].view(np.uint32))
+    np.testing.assert_array_equal(to_bits(q), o["q"])
+    assert not np.isfinite(o["s"]).all() or (o["q"] == 0xFE).any()
+
+
 @pytest.mark.parametrize("rows,K", [(1, 16), (7, 2048), (8192, 2048), (5, 2064), (3, 4096),
                                     (9, 8192), (2, 16384), (4, 6144)])
 def test_rowquant_bit_exact(rows, K, cuda_dev):
