@@ -130,13 +130,22 @@ rowquant_kernel(const RowquantArgs a) {
     // Exact amax over the candidates (see the file comment).  A thread whose
     // own fast maximum is below the threshold holds no candidate; the rare
     // candidates re-read their input element.
+    // A fast maximum of +inf comes from an input of +inf only (the fast GELU
+    // of a finite input is finite, its exact value too), whose canonical GELU
+    // is +inf: the exact maximum is +inf, and the threshold below would be
+    // NaN.  amax is the group's, so the whole group takes the same branch.
+    const bool inf_row = amax > 3.402823466e38f;
     const float margin = __fmaf_rn(amax, 0x1p-11f, 0x1p-19f);
     const float thresh = amax - margin;
-    float exact = 0.0f;
-    if (lamax >= thresh) {
+    float exact = inf_row ? amax : 0.0f;
+    // Only elements of the row are candidates: a chunk past the row's end
+    // (e >= K) or a row past the last holds zeros, which pass a negative
+    // threshold (a row of tiny values) but have no input to re-read.
+    if (!inf_row && row_ok && lamax >= thresh) {
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {
         const int e = (t + 32 * GROUP * c) * 16;
+        if (e >= K) continue;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           const float yk = (k & 1) ? f2hi(y2[c][k >> 1]) : f2lo(y2[c][k >> 1]);

@@ -251,6 +251,44 @@ def test_rowquant_gelu_scale_exact_codes_at_ties(rows, K, outliers, cuda_dev):
     _codes_at_ties_only(to_bits(q), oy, os_)
 
 
+@pytest.mark.parametrize("K", [8192, 2048, 16384, 1024, 16])
+def test_rowquant_gelu_exhaustive(K, cuda_dev):
+    """Every finite bf16 input, in rows of K inputs of neighbouring magnitude
+    (both signs, shuffled within the row, zero padding), so that each row's
+    codes span the e4m3 range, and (K >= 128) the non-finite rows of
+    _nonfinite_rows, +inf and -inf included: GELU scales bit-exact against
+    the oracle, codes equal to the oracle's except where y/s lies within 4
+    fp32 ulp of an e4m3 rounding tie."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    vals = (bits.astype(np.uint32) << 16).view(np.float32)
+    fin = bits[np.isfinite(vals)]
+    fin = fin[np.argsort(fin & 0x7FFF, kind="stable")]
+    pad = (-fin.size) % K
+    x = np.concatenate([fin, np.zeros(pad, np.uint16)]).reshape(-1, K)
+    r = rng(K)
+    for row in x:
+        r.shuffle(row)
+    x = x[None]
+    if K >= 128:
+        x = np.concatenate([x, _nonfinite_rows(K)], axis=1)
+    q, s = afb.rowquant(dev(x, cuda_dev), gelu=True)
+    oq, os_, oy = C.rowquant(x, gelu=True, want_y=True)
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), os_.view(np.uint32))
+    qb = to_bits(q).reshape(oq.shape)
+    bad = qb != oq
+    if bad.any():
+        rows = os_.shape[0]
+        with np.errstate(invalid="ignore"):  # rows of +inf: inf / inf where the codes agree
+            v = (oy.reshape(rows, -1) / os_.reshape(rows, 1)).astype(np.float32).reshape(oq.shape)[bad]
+        assert np.all(np.isfinite(v)), "a code differs where the quotient is not finite"
+        lo, hi = v.copy(), v.copy()
+        for _ in range(4):
+            lo = np.nextafter(lo, -np.inf, dtype=np.float32)
+            hi = np.nextafter(hi, np.inf, dtype=np.float32)
+        c = lambda a: torch.from_numpy(np.clip(a, -448, 448)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+        assert np.all(c(lo) != c(hi)), "an FP8 code differs away from a rounding tie"
+
+
 def test_gelu_probe_exhaustive(cuda_dev):
     """Over all finite bf16 inputs: the device canonical GELU equals the
     oracle's bit for bit, and the fast GELU stays within the bound the row
