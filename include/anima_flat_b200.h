@@ -178,8 +178,8 @@ int afb_silu_probe(void* stats, void* stream);
  * anima_flat::residual_adaln_bwd op, launching _residual_adaln_bwd_kernel,
  * adaln.py:111-172).  gz may be NULL.  Outputs, in the op's order: dx, dres
  * [batch, seq, dim]; dgate, dshift, dscale [batch, dim] bf16.  dim <= 2048.
- * Workspace: batch * ceil(seq / 32) * 3 * dim * 4 bytes (chunk partials of
- * 32 rows). */
+ * Workspace: batch * ceil(seq / 28) * 3 * dim * 4 bytes (chunk partials of
+ * 28 rows). */
 size_t afb_residual_adaln_bwd_workspace(int64_t batch, int64_t seq, int64_t dim);
 int afb_residual_adaln_bwd(const void* gh, const void* gz, const void* z, const void* x,
                            const void* gate, const void* scale, void* dx, void* dres,
@@ -193,7 +193,7 @@ int afb_residual_adaln_bwd(const void* gh, const void* gz, const void* z, const 
  * hot path).  It has no counterpart in the reference.  Same arguments and
  * outputs, without the workspace: the partial sums live in a 16 MiB array
  * inside the library, which every GPU that loads the library holds until
- * exit.  Sizes needing more (batch * ceil(seq / 32) * 3 * dim * 4 bytes, the
+ * exit.  Sizes needing more (batch * ceil(seq / 28) * 3 * dim * 4 bytes, the
  * workspace query's value) are rejected, overflowing sizes included.  The
  * first call on a device resolves the array's address and caches it, so make
  * it before any stream capture, and do not call cudaDeviceReset while the

@@ -143,11 +143,11 @@ def gelu(x_bits: np.ndarray) -> np.ndarray:
 
 
 # Chunk geometry of the CUDA backward kernels (csrc/adaln_bwd.cu, headnorm_bwd.cu):
-# it fixes the order of the parameter-gradient sums.  AdaLN: chunks of 32 rows,
+# it fixes the order of the parameter-gradient sums.  AdaLN: chunks of 28 rows,
 # each column summed over the chunk's rows in increasing order from zero (one
-# stream of 32 rows).
+# stream of 28 rows).
 BWD_WARPS = 1
-BWD_ROWS_PER_WARP = 32
+BWD_ROWS_PER_WARP = 28
 HN_WARPS = 8
 HN_TOK_PER_WARP = 1
 

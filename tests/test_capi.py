@@ -39,8 +39,8 @@ def test_signature_table_covers_compute_entry_points():
 
 def test_workspace_queries():
     lib = _lib.load()
-    # [B][chunks of 32 rows][3][D] fp32 (the row scalars stay in shared memory)
-    assert lib.afb_residual_adaln_bwd_workspace(1, 4096, 2048) == 1 * 128 * 3 * 2048 * 4
+    # [B][chunks of 28 rows][3][D] fp32 (the row scalars stay in shared memory)
+    assert lib.afb_residual_adaln_bwd_workspace(1, 4096, 2048) == 1 * 147 * 3 * 2048 * 4
     assert lib.afb_adaln_bwd_workspace(2, 17, 256) == 2 * 1 * 2 * 256 * 4
     # sizes whose workspace does not fit in size_t report SIZE_MAX instead of wrapping
     assert lib.afb_residual_adaln_bwd_workspace(2**62, 2**40, 2048) == 2**64 - 1

@@ -19,7 +19,7 @@ from tests.test_gpu_forward import act, mods, qkv_inputs, rng
 pytestmark = pytest.mark.gpu
 
 
-# (2, 33000, 256): more than 1024 chunks of 32 rows per batch entry, so the
+# (2, 33000, 256): more than 1024 chunks of 28 rows per batch entry, so the
 # parameter gradients take the two-launch finalize, with two batch entries.
 @pytest.mark.parametrize("B,S,D", [(1, 4096, 2048), (2, 37, 2048), (1, 5, 256), (3, 17, 1024),
                                    (1, 1, 2048), (2, 33, 2040), (2, 33000, 256)])

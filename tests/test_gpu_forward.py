@@ -289,6 +289,29 @@ def test_rowquant_gelu_exhaustive(K, cuda_dev):
         assert np.all(c(lo) != c(hi)), "an FP8 code differs away from a rounding tie"
 
 
+@pytest.mark.parametrize("K", [8192, 2048, 16])
+def test_rowquant_exhaustive_bit_exact(K, cuda_dev):
+    """Without GELU: every finite bf16 input, in rows of neighbouring
+    magnitude as above, and (K >= 128) the non-finite rows: codes and scales
+    bit-exact against the oracle."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    vals = (bits.astype(np.uint32) << 16).view(np.float32)
+    fin = bits[np.isfinite(vals)]
+    fin = fin[np.argsort(fin & 0x7FFF, kind="stable")]
+    pad = (-fin.size) % K
+    x = np.concatenate([fin, np.zeros(pad, np.uint16)]).reshape(-1, K)
+    r = rng(K + 1)
+    for row in x:
+        r.shuffle(row)
+    x = x[None]
+    if K >= 128:
+        x = np.concatenate([x, _nonfinite_rows(K)], axis=1)
+    q, s = afb.rowquant(dev(x, cuda_dev), gelu=False)
+    oq, os_ = C.rowquant(x)
+    np.testing.assert_array_equal(to_bits(s).view(np.uint32), os_.view(np.uint32))
+    np.testing.assert_array_equal(to_bits(q), oq)
+
+
 def test_gelu_probe_exhaustive(cuda_dev):
     """Over all finite bf16 inputs: the device canonical GELU equals the
     oracle's bit for bit, and the fast GELU stays within the bound the row
