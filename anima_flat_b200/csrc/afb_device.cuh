@@ -740,7 +740,7 @@ __device__ __forceinline__ f2_t splat2(float v) { return f2(v, v); }
 __device__ __forceinline__ f2_t fast_gelu2(f2_t x) {
   constexpr f2_t kAbs = 0x7fffffff7fffffffull;
   const f2_t hx = mul2(x, splat2(0.5f));
-  const f2_t hax = mul2(x & kAbs, splat2(0.5f));
+  const f2_t hax = hx & kAbs;  // |x / 2| = |x| / 2 exactly (halving rounds symmetrically)
   const f2_t den = fma2(hax, splat2(2.0f * (0.3275911f * 0.707106769084930419921875f)), splat2(1.0f));
   float t0, t1;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(f2lo(den)));
