@@ -130,6 +130,7 @@ __host__ __device__ constexpr size_t bwd_slot_bytes(int64_t dim, bool has_x) {
 }
 __host__ __device__ constexpr size_t bwd_smem(int64_t dim, int nt, bool has_x, int ns) {
   return static_cast<size_t>(ns) * (bwd_stage_bytes(dim, nt) + kStageRows * sizeof(float4) + 3 * sizeof(uint64_t)) +
+         kBwdModSlots * sizeof(uint64_t) +
          kBwdModSlots * bwd_slot_bytes(dim, has_x) + kBwdXchBytes;
 }
 
@@ -191,6 +192,13 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
   uint64_t* full = reinterpret_cast<uint64_t*>(xch_all + kBwdPairs * kBwdXchF2);
   uint64_t* ready = full + ns;
   uint64_t* empty = ready + ns;
+  // The modulation rows of chunk k land in slot k & 1 on mfull[k & 1], whose
+  // phase for chunk k has parity (k >> 1) & 1.  Both row-pair groups wait on
+  // it once per chunk before reading the slot: the rows are issued with the
+  // chunk's first stage, which one group does not take (the groups take
+  // alternate stages), so that stage's barrier cannot carry them.  The
+  // column warps are ordered after it through the first stage's ready.
+  uint64_t* mfull = empty + ns;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t my_units =
@@ -203,6 +211,7 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
       mbar_init(smem_addr(&ready[s]), 2 * kStageRows);  // the warps of one pair group
       mbar_init(smem_addr(&empty[s]), kBwdColWarps);
     }
+    for (int m = 0; m < kBwdModSlots; ++m) mbar_init(smem_addr(&mfull[m]), 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -250,10 +259,15 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
       return EXACT ? __fmul_rn(v, 1.0f / (NC * 256)) : __fdiv_rn(v, static_cast<float>(D));
     };
     bool dead = false;
+    int mchunk = -1;  // the chunk whose modulation rows this warp has waited for
     for (int64_t j = 0; j < nstages; ++j, cur.next(a, ns)) {
       if (static_cast<int>(j % kBwdRowGroups) != group) continue;
       const int s = cur.slot;
       if (!dead && !mbar_wait(smem_addr(&full[s]), cur.parity)) dead = true;
+      if (!dead && cur.k != mchunk) {
+        if (!mbar_wait(smem_addr(&mfull[cur.k & 1]), static_cast<uint32_t>((cur.k >> 1) & 1))) dead = true;
+        mchunk = cur.k;
+      }
       if (dead) continue;  // no arrival: the column warps' bounded waits give up too
       if (prow < cur.n) {
         const uint8_t* zr = smem + static_cast<size_t>(s) * stage_bytes + static_cast<size_t>(prow) * D * 2;
@@ -301,10 +315,11 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
   if (warp == kBwdProducerWarp) {
     // ---------------- producer: stream the stages into the ring ------------
     // Stage j goes into slot j % ns once the column warps have released the
-    // stage that held it before (j - ns), with the modulation rows of its
-    // chunk ahead of a chunk's first stage.
+    // stage that held it before (j - ns); a chunk's modulation rows go
+    // with its first stage, on their own barrier (mfull).
     if (lane != 0) return;
     bool dead = false;
+    int mod_k = -1;  // the last chunk whose modulation rows were issued
     int64_t j = 0;
     for (; j < nstages; ++j, cur.next(a, ns)) {
       const uint32_t bar = smem_addr(&full[cur.slot]);
@@ -323,13 +338,15 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
       const uint32_t row_bytes = static_cast<uint32_t>(D * 2);
       const uint32_t dst = smem_addr(smem + static_cast<size_t>(cur.slot) * stage_bytes);
       const int64_t off = cur.row0 * D;
-      const bool first = cur.i == 0;
-      mbar_arrive_expect_tx(bar, NT * bytes + (first ? (HAS_X ? 2u : 1u) * row_bytes : 0u));
-      if (first) {
+      if (cur.i == 0) {  // a chunk's first stage: its modulation rows, on their own barrier
+        const uint32_t mb = smem_addr(&mfull[cur.k & 1]);
         const uint32_t slot = smem_addr(mods + (cur.k & 1) * slot_bytes);
-        bulk_g2s(slot, a.scale + cur.b * D, row_bytes, bar);
-        if (HAS_X) bulk_g2s(slot + row_bytes, a.gate + cur.b * D, row_bytes, bar);
+        mbar_arrive_expect_tx(mb, (HAS_X ? 2u : 1u) * row_bytes);
+        bulk_g2s(slot, a.scale + cur.b * D, row_bytes, mb);
+        if (HAS_X) bulk_g2s(slot + row_bytes, a.gate + cur.b * D, row_bytes, mb);
+        mod_k = cur.k;
       }
+      mbar_arrive_expect_tx(bar, NT * bytes);
       bulk_g2s(dst, a.z + off, bytes, bar);
       bulk_g2s(dst + tensor_bytes, a.gh + off, bytes, bar);
       if (HAS_GZ) bulk_g2s(dst + 2 * tensor_bytes, a.gz + off, bytes, bar);
@@ -338,6 +355,8 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
     if (dead) {  // drain the copies issued before the failed wait (bounded waits)
       for (int64_t k = j - ns; k < j; ++k)
         if (k >= 0) mbar_wait(smem_addr(&full[k % ns]), static_cast<uint32_t>((k / ns) & 1));
+      for (int k = mod_k - 1; k <= mod_k; ++k)
+        if (k >= 0) mbar_wait(smem_addr(&mfull[k & 1]), static_cast<uint32_t>((k >> 1) & 1));
     }
     return;
   }
@@ -355,6 +374,9 @@ adaln_bwd_kernel(const AdalnBwdArgs a, const int ns) {
     const int s = cur.slot;
     if (!dead && !(mbar_wait(smem_addr(&full[s]), cur.parity) && mbar_wait(smem_addr(&ready[s]), cur.parity)))
       dead = true;
+    // The chunk's modulation rows need no wait of their own here: the first
+    // stage's row pair group waits for them (mfull) before its arrival on
+    // ready, which this warp has just waited for.
     if (cur.i == 0) {
 #pragma unroll
       for (int v = 0; v < kColVecs; ++v) {

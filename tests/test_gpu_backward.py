@@ -40,6 +40,29 @@ def test_residual_adaln_bwd_bit_exact(B, S, D, has_gz, cuda_dev):
     np.testing.assert_array_equal(to_bits(dscale), o["dscale"])
 
 
+@pytest.mark.parametrize("S", [28, 30])
+def test_residual_adaln_bwd_many_batch_entries(S, cuda_dev):
+    """Short sequences, so that nearly every 28-row chunk starts a new batch
+    entry and needs its own scale and gate rows in the modulation slot; five
+    calls in a row, bit-exact every time.  Each row-pair group must wait for
+    the chunk's modulation rows before reading them, whichever stage carries
+    them."""
+    B, D = 256, 2048
+    r = rng(S + 4242)
+    z, x = act(r, (B, S, D)), act(r, (B, S, D))
+    gh, gz = act(r, (B, S, D), std=1e-2), act(r, (B, S, D), std=1e-2)
+    _, scale, gate = mods(r, B, D)
+    t = lambda a: from_bits(a, cuda_dev)
+    o = C.adaln_bwd(gh, z, scale, x=x, gate=gate, gz=gz)
+    args = [t(gh), t(gz), t(z), t(x), t(gate), t(scale)]
+    for _ in range(5):
+        dx, dres, dgate, dshift, dscale = torch.ops.anima_flat_b200.residual_adaln_bwd(*args, 1e-6)
+        np.testing.assert_array_equal(to_bits(dres), o["dz"])
+        np.testing.assert_array_equal(to_bits(dx), o["dx"])
+        np.testing.assert_array_equal(to_bits(dgate), o["dgate"])
+        np.testing.assert_array_equal(to_bits(dscale), o["dscale"])
+
+
 @pytest.mark.parametrize("B,S,D", [(1, 4096, 2048), (2, 19, 512)])
 def test_adaln_bwd_bit_exact(B, S, D, cuda_dev):
     r = rng(B * 200 + S + D)
