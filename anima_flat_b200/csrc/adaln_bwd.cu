@@ -20,10 +20,11 @@
 // One persistent kernel does all the per-row work.  A CTA (one per SM) owns
 // the chunks blockIdx.x, blockIdx.x + gridDim.x, ... and streams them through
 // a ring of shared-memory stages, kStageRows = 2 rows of every input tensor
-// (z, gh, and gz, x where present) per stage, with the chunk's scale (and
-// gate) rows in two modulation slots, filled by bulk copies (TMA engine)
-// that complete on the stage's mbarrier.  So every input byte crosses HBM
-// once and is then read from shared memory by three warp roles:
+// (z, gh, and gz, x where present) per stage, filled by bulk copies (TMA
+// engine) that complete on the stage's mbarrier, and the chunk's scale (and
+// gate) rows in two modulation slots, whose copies complete on a barrier of
+// their own per slot.  So every input byte crosses HBM once and is then read
+// from shared memory by three warp roles:
 //  - a producer warp issues the bulk copies of each stage once the column
 //    warps have released its slot (an issuing thread can block for a
 //    microsecond on a full copy queue, so no compute warp issues them);
@@ -121,7 +122,7 @@ __host__ __device__ constexpr int bwd_tensors() { return 2 + (HAS_GZ ? 1 : 0) + 
 // modulation slots (the scale row, and the gate row with HAS_X, of a chunk's
 // batch entry); the row scalars of each stage; the row pairs' exchange
 // buffers; three mbarriers per stage (data full, scalars ready, stage
-// empty).
+// empty) and one per modulation slot (rows landed).
 __host__ __device__ constexpr size_t bwd_stage_bytes(int64_t dim, int nt) {
   return static_cast<size_t>(nt) * kStageRows * static_cast<size_t>(dim) * 2;
 }
